@@ -1,0 +1,581 @@
+"""Benchmark of the B200 paged-KV attention path (nvattn).
+
+Headline (the first part of BASELINE.json's metric, "paged decode-attn HBM
+GB/s"): configs[3], long-context paged decode at the Qwen3-32B attention shape
+(64 Q / 8 KV heads, head_dim 128, bf16 cache, 256-token blocks, 128 sequences,
+context lengths uniform in [4096, 32768], physical blocks randomly permuted).
+One step = one decode-mode ``Attention.forward`` (nanovllm/layers/attention.py
+:59-75): KV scatter of the new token + split-K paged decode (+ combine).
+Heads are sharded across ranks like the engine's tensor parallelism
+(qwen3.py:29-35): with N GPUs each rank owns 8/N KV heads and 64/N Q heads of
+the same batch (strong scaling: the total work is fixed).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nvattn|reference]
+
+Rank 0 prints one JSON line. ``value`` is the whole-job algorithmic HBM
+throughput (bytes all ranks must move / max-over-ranks device time) with
+inputs resident in HBM; ``e2e`` is the same metric through the public API
+with the step's inputs copied from pinned host memory and the output copied
+back inside the timed region. Secondary lines in the same JSON: prefill
+TFLOP/s at configs[2] (prefix-cached prefill, Qwen3-8B shape) and tree
+verification at configs[4].
+
+``--impl reference`` times the reference's attention math as a CPU
+restatement (the oracle; the reference's own attention is flash-attn CUDA
+code with no CPU path) on all host cores, on a bounded sample of the same
+workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "nano-vllm-x_b200"))
+
+H_TOTAL, KVH_TOTAL, D, BS = 64, 8, 128, 256
+BATCH, CTX_LO, CTX_HI = 128, 4096, 32768
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+METRIC = "paged decode-attn HBM GB/s"
+WORKLOAD = ("configs[3] long-context paged decode, Qwen3-32B attention: 64Q/8KV heads, d128, "
+            "bf16 KV cache, 256-token blocks, 128 seqs, ctx U[4096,32768], permuted blocks; "
+            "step = Attention.forward decode (KV scatter + split-K decode + combine)")
+
+
+# ----------------------------------------------------------------- workload
+
+def decode_workload(seed: int = 0):
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int32)
+    nblk = (lens + BS - 1) // BS
+    total = int(nblk.sum())
+    perm = rng.permutation(total).astype(np.int32)
+    width = int(nblk.max())
+    bt = np.full((BATCH, width), -1, np.int32)
+    pos = 0
+    for b in range(BATCH):
+        bt[b, :nblk[b]] = perm[pos:pos + nblk[b]]
+        pos += nblk[b]
+    return lens, bt, total
+
+
+def decode_bytes(lens, kvh, h):
+    """Algorithmic HBM bytes of one decode step on one rank."""
+    kv_read = int(lens.astype(np.int64).sum()) * kvh * D * 2 * 2
+    qo = 2 * len(lens) * h * D * 2
+    scatter = 2 * len(lens) * kvh * D * 2 * 2  # read new k/v + write to the cache
+    meta = len(lens) * 4 * 2 + int(((lens + BS - 1) // BS).sum()) * 4
+    return kv_read + qo + scatter + meta
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), float(
+            j.get("bf16_tflops_sustained", j["bf16_tflops"])), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, 1400.0, "fallback"
+
+
+# ------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock + throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "100"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# -------------------------------------------------------------- distributed
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------- nvattn arm
+
+def timed(fn, steps, stream):
+    """Device time (ms) of `steps` calls of fn on `stream`, CUDA events."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
+def run_nvattn(args):
+    import nvattn
+    from nvattn import context as ctxmod
+    from nvattn import ops
+    from nvattn.parallel import head_shard
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    (q0, q1), (k0, k1) = head_shard(H_TOTAL, KVH_TOTAL, rank, world)
+    H, KVH = q1 - q0, k1 - k0
+    hbm_peak, tf_peak, tf_sus, peak_src = load_peaks()
+
+    lens, bt_np, nblocks = decode_workload(0)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    kv = torch.empty(2, nblocks, BS, KVH, D, dtype=torch.bfloat16, device=dev)
+    kv.normal_(generator=g)
+    k_cache, v_cache = kv[0], kv[1]
+    attn = nvattn.Attention(H, D, D ** -0.5, KVH)
+    attn.k_cache, attn.v_cache = k_cache, v_cache
+
+    # decode inputs: the new token of every sequence sits at position len-1
+    ctx_lens = lens.copy()
+    slots = np.array([bt_np[b, (n - 1) // BS] * BS + (n - 1) % BS for b, n in enumerate(lens)],
+                     np.int32)
+    q = torch.randn(BATCH, H, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(BATCH, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(BATCH, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    slot_d = torch.from_numpy(slots).to(dev)
+    lens_d = torch.from_numpy(ctx_lens).to(dev)
+    bt_d = torch.from_numpy(bt_np).to(dev)
+    ws = torch.empty(max(1, ops.decode_workspace_bytes(BATCH, H, KVH, bt_np.shape[1], BS)),
+                     dtype=torch.uint8, device=dev)
+    ops.status_tensor(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ctxmod.set_context(False, slot_mapping=slot_d, context_lens=lens_d, block_tables=bt_d)
+        attn(q, k, v)
+
+    def decode_only():
+        ops.paged_decode(q, k_cache, v_cache, lens_d, bt_d, softmax_scale=D ** -0.5,
+                         workspace=ws)
+
+    nsplit_launches = 2 if ops.decode_workspace_bytes(BATCH, H, KVH, bt_np.shape[1], BS) else 1
+    bytes_rank = decode_bytes(lens, KVH, H)
+    bytes_decode = bytes_rank - 2 * BATCH * KVH * D * 2 * 2  # without the scatter
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier(world)
+    ms = timed(step, args.steps, stream)
+    barrier(world)
+    ms_dec = timed(decode_only, args.steps, stream)
+    clocks = sampler.stop()
+    st = ops.read_status(dev)
+    if st:
+        raise SystemExit(f"kernel status word {st} (bad slot/block or timeout)")
+
+    # ---- e2e through the public API with host buffers
+    pin = lambda a: torch.from_numpy(a).pin_memory()  # noqa: E731
+    q_h = q.cpu().pin_memory()
+    k_h = k.cpu().pin_memory()
+    v_h = v.cpu().pin_memory()
+    slot_h, lens_h, bt_h = pin(slots), pin(ctx_lens), pin(bt_np)
+    out_h = torch.empty(BATCH, 1, H, D, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, slot_h, lens_h, bt_h))
+    d2h = out_h.numel() * out_h.element_size()
+
+    def e2e_step():
+        qd = q_h.to(dev, non_blocking=True)
+        kd = k_h.to(dev, non_blocking=True)
+        vd = v_h.to(dev, non_blocking=True)
+        ctxmod.set_context(False, slot_mapping=slot_h.to(dev, non_blocking=True),
+                           context_lens=lens_h.to(dev, non_blocking=True),
+                           block_tables=bt_h.to(dev, non_blocking=True))
+        o = attn(qd, kd, vd)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_e2e = timed(e2e_step, args.steps, stream)
+    ctxmod.reset_context()
+
+    t_step = max_over_ranks(ms / args.steps, world)
+    t_dec = max_over_ranks(ms_dec / args.steps, world)
+    t_e2e = max_over_ranks(ms_e2e / args.steps, world)
+    total_bytes = sum_over_ranks(bytes_rank, world)
+    value = total_bytes / (t_step * 1e-3) / 1e9
+    e2e_value = total_bytes / (t_e2e * 1e-3) / 1e9
+    achieved = bytes_decode / (t_dec * 1e-3) / 1e9
+
+    secondary = {}
+    if not args.skip_secondary:
+        del kv, k_cache, v_cache
+        attn.k_cache = attn.v_cache = torch.tensor([])
+        torch.cuda.empty_cache()
+        secondary["prefill_cfg3"] = bench_prefill(dev, rank, world, args, tf_peak)
+        secondary["tree_verify_cfg5"] = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
+        if rank == 0 and world == 1:
+            secondary["flash_attn_decode_cfg4"] = bench_flash_attn_decode(dev, args, H, KVH)
+
+    traffic = None
+    prof = REPO / "profiles" / "paged_decode_cfg4.json"
+    if prof.exists():
+        try:
+            traffic = json.loads(prof.read_text()).get(f"traffic_bytes_per_launch_tp{world}")
+        except (ValueError, OSError):
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_decode_sample(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(t_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) bf16 K/V/Q; numpy seed 0 lengths and block permutation)",
+            "config": {"workload": WORKLOAD, "global_batch": BATCH, "num_heads": H_TOTAL,
+                       "num_kv_heads": KVH_TOTAL, "head_dim": D, "block_size": BS,
+                       "ctx_range": [CTX_LO, CTX_HI], "parallelism": f"tp{world} (head-sharded)",
+                       "l2": "inputs larger than L2 (KV cache >= 1.2 GB per rank vs 126 MB L2)"},
+            "frac_of_nominal_8tbs": round(value / world / NOMINAL_HBM_GBS, 4),
+            "roofline": {"kernel": "paged_decode (split-K kernel + combine)", "bound": "hbm",
+                         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": bytes_decode,
+                         "ms_per_launch": round(t_dec, 4)},
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(t_e2e, 4)},
+            "gpu_launches": args.steps * (1 + nsplit_launches),
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def bench_prefill(dev, rank, world, args, tf_peak):
+    """64 seqs share a 2048-token prefix (8 cached blocks), suffix U[128,512]."""
+    from nvattn import ops
+    from nvattn.parallel import head_shard
+    (q0, q1), (k0, k1) = head_shard(32, 8, rank, world)
+    H, KVH = q1 - q0, k1 - k0
+    rng = np.random.default_rng(3)
+    B, P = 64, 2048
+    suf = rng.integers(128, 513, size=B).astype(np.int64)
+    klen = P + suf
+    pre_blocks = P // BS
+    own = (suf + BS - 1) // BS
+    nblocks = pre_blocks + int(own.sum())
+    width = pre_blocks + int(own.max())
+    bt = np.full((B, width), -1, np.int32)
+    pos = pre_blocks
+    for b in range(B):
+        bt[b, :pre_blocks] = np.arange(pre_blocks)
+        bt[b, pre_blocks:pre_blocks + own[b]] = np.arange(pos, pos + own[b])
+        pos += own[b]
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    kc = torch.randn(nblocks, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(nblocks, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(int(suf.sum()), H, D, generator=g, device=dev).to(torch.bfloat16)
+    cq = torch.tensor(np.concatenate([[0], np.cumsum(suf)]), dtype=torch.int32, device=dev)
+    ck = torch.tensor(np.concatenate([[0], np.cumsum(klen)]), dtype=torch.int32, device=dev)
+    btd = torch.from_numpy(bt).to(dev)
+    out = torch.empty_like(q)
+    flops = float(sum(4 * D * H * (P + i + 1) for s in suf for i in range(int(s))))
+
+    def fn():
+        ops.varlen_prefill(q, kc, vc, cq, ck, int(suf.max()), int(klen.max()),
+                           softmax_scale=D ** -0.5, causal=True, block_table=btd, out=out)
+
+    for _ in range(args.warmup):
+        fn()
+    barrier(world)
+    ms = max_over_ranks(timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps,
+                        world)
+    total = sum_over_ranks(flops, world)
+    tfs = total / (ms * 1e-3) / 1e12
+    return {"metric": "prefill attn TFLOP/s", "value": round(tfs, 1), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4),
+            "frac_of_measured_bf16_peak_per_gpu": round(tfs / world / tf_peak, 4),
+            "flops_per_step": total,
+            "workload": "configs[2]: 64 seqs, 2048-token shared prefix (8 blocks), suffix "
+                        "U[128,512], 32Q/8KV, d128, causal over prefix+suffix"}
+
+
+def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
+    """32 seqs, ctx U[1024,8192], 64-node EAGLE tree (depth 6)."""
+    from nvattn import ops, tree
+    from nvattn.parallel import head_shard
+    (q0, q1), (k0, k1) = head_shard(32, 8, rank, world)
+    H, KVH = q1 - q0, k1 - k0
+    rng = np.random.default_rng(5)
+    B, N = 32, 64
+    ctx = rng.integers(1024, 8193, size=B).astype(np.int64)
+    parents, depths = tree.build_draft_tree((4, 3, 2, 1, 1, 1), N)
+    masks = tree.ancestor_masks(parents)
+    tot = ctx + N
+    nblk = (tot + BS - 1) // BS
+    nblocks = int(nblk.sum())
+    perm = rng.permutation(nblocks).astype(np.int32)
+    bt = np.full((B, int(nblk.max())), -1, np.int32)
+    pos = 0
+    for b in range(B):
+        bt[b, :nblk[b]] = perm[pos:pos + nblk[b]]
+        pos += nblk[b]
+    g = torch.Generator(device=dev).manual_seed(99 + rank)
+    kc = torch.randn(nblocks, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(nblocks, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(B * N, H, D, generator=g, device=dev).to(torch.bfloat16)
+    cq = torch.arange(0, (B + 1) * N, N, dtype=torch.int32, device=dev)
+    ctx_d = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    m_d = torch.from_numpy(np.tile(masks, B).view(np.int64)).to(dev)
+    btd = torch.from_numpy(bt).to(dev)
+    out = torch.empty_like(q)
+    n_anc = np.array([bin(int(x)).count("1") for x in masks])
+    flops = float(sum(4 * D * H * (int(c) + int(a)) for c in ctx for a in n_anc))
+    nbytes = float(int(tot.sum()) * KVH * D * 2 * 2 + 2 * B * N * H * D * 2)
+
+    def fn():
+        ops.tree_attention(q, kc, vc, cq, ctx_d, m_d, btd, N, softmax_scale=D ** -0.5, out=out)
+
+    for _ in range(args.warmup):
+        fn()
+    barrier(world)
+    ms = max_over_ranks(timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps,
+                        world)
+    tf = sum_over_ranks(flops, world) / (ms * 1e-3) / 1e12
+    gbs = sum_over_ranks(nbytes, world) / (ms * 1e-3) / 1e9
+    return {"metric": "tree-verify attn TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
+            "GB_per_s": round(gbs, 1), "ms_per_step": round(ms, 4),
+            "frac_of_measured_bf16_peak_per_gpu": round(tf / world / tf_peak, 4),
+            "frac_of_measured_hbm_per_gpu": round(gbs / world / hbm_peak, 4),
+            "workload": "configs[4]: 32 seqs, ctx U[1024,8192], 64-node tree (branching "
+                        "[4,3,2,1,1,1], depth 6), 32Q/8KV, d128"}
+
+
+def bench_flash_attn_decode(dev, args, H, KVH):
+    """The reference's own GPU decode call (flash-attn, attention.py:72-74) on the
+    same workload, for comparison; reports why if it cannot run."""
+    try:
+        from flash_attn import flash_attn_with_kvcache
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flash-attn import failed: {e!r}"[:200]}
+    try:
+        lens, bt_np, nblocks = decode_workload(0)
+        g = torch.Generator(device=dev).manual_seed(5)
+        kc = torch.randn(nblocks, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+        vc = torch.randn(nblocks, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+        q = torch.randn(BATCH, 1, H, D, generator=g, device=dev).to(torch.bfloat16)
+        lens_d = torch.from_numpy(lens).to(dev)
+        bt_d = torch.from_numpy(bt_np).to(dev)
+
+        def fn():
+            flash_attn_with_kvcache(q, kc, vc, cache_seqlens=lens_d, block_table=bt_d,
+                                    softmax_scale=D ** -0.5, causal=True)
+
+        for _ in range(args.warmup):
+            fn()
+        ms = timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+        nbytes = decode_bytes(lens, KVH, H) - 2 * BATCH * KVH * D * 2 * 2
+        return {"impl": "flash-attn (reference GPU path)", "value": round(nbytes / ms / 1e6, 1),
+                "unit": "GB/s", "ms_per_step": round(ms, 4)}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flash-attn did not run: {e!r}"[:200]}
+
+
+# ---------------------------------------------------------- CPU baseline
+
+def cpu_decode_sample(budget_s: float):
+    """Oracle decode (reference attention math on CPU) over a bounded sample of
+    the workload's sequences; all host threads."""
+    sys.path.insert(0, str(REPO))
+    from oracle import reference_math as R
+    lens, _, _ = decode_workload(0)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(4321)
+    done_bytes, t_total, n = 0, 0.0, 0
+    for b in range(BATCH):
+        L = int(lens[b])
+        nb = (L + BS - 1) // BS
+        kc = torch.randn(nb, BS, KVH_TOTAL, D, generator=gen).to(torch.bfloat16)
+        vc = torch.randn(nb, BS, KVH_TOTAL, D, generator=gen).to(torch.bfloat16)
+        q = torch.randn(1, H_TOTAL, D, generator=gen).to(torch.bfloat16)
+        bt = np.arange(nb, dtype=np.int32).reshape(1, nb)
+        t0 = time.perf_counter()
+        R.decode_attention(q, kc, vc, np.array([L]), bt, D ** -0.5)
+        t_total += time.perf_counter() - t0
+        done_bytes += L * KVH_TOTAL * D * 2 * 2
+        n += 1
+        if t_total > budget_s and n >= 2:
+            break
+    return {"value": round(done_bytes / t_total / 1e9, 3), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"{n} of {BATCH} sequences of the workload (all 64Q/8KV heads), "
+                      f"{t_total:.1f} s of CPU time, torch fp32 restatement (oracle)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # the CPU reference runs on rank 0 only
+    for _ in range(args.warmup):
+        pass
+    vals, last = [], None
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps)):
+        last = cpu_decode_sample(args.cpu_seconds / max(1, args.steps))
+        vals.append(last["value"])
+    value = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round((time.perf_counter() - t0) * 1e3 / max(1, args.steps), 2),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "global_batch": BATCH, "num_heads": H_TOTAL,
+                   "num_kv_heads": KVH_TOTAL, "head_dim": D, "block_size": BS,
+                   "parallelism": "cpu (host cores)"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": last["cores"],
+                         "kind": "port", "sample": last["sample"]},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("nvattn", "reference"), default="nvattn")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--skip-secondary", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_nvattn(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,213 @@
+/*
+ * nvattn — B200 (sm_100a) paged-KV attention for Nano-vLLM-X, C ABI.
+ *
+ * This is the drop-in boundary for the attention hot path of Nano-vLLM-X
+ * (nanovllm/layers/attention.py). The reference reaches three GPU routines
+ * from that file; each entry point below replaces one of them with the same
+ * argument meaning:
+ *
+ *   store_kvcache_kernel / store_kvcache   attention.py:10-40  -> nvattn_store_kvcache
+ *   flash_attn_varlen_func (dense, paged)  attention.py:64-70  -> nvattn_varlen_prefill
+ *   flash_attn_with_kvcache (decode)       attention.py:71-74  -> nvattn_paged_decode
+ *
+ * plus two entry points with no counterpart in the reference, for EAGLE-style
+ * speculative verification over the same cache layout:
+ *
+ *   nvattn_tree_verify   ancestor-masked attention of draft-tree nodes
+ *   nvattn_kv_move       compaction of the accepted path's K/V slots
+ *
+ * Conventions (all entry points):
+ *   - Pointers are device pointers unless stated otherwise; no torch types.
+ *   - Strides are in ELEMENTS (like torch.Tensor.stride()).
+ *   - Element type is bf16 (2 bytes); head_dim must be 128.
+ *   - KV cache layout is the engine's (nanovllm/engine/model_runner.py:115):
+ *     one layer's cache is [num_blocks][block_size][num_kv_heads][head_dim],
+ *     contiguous; slot s lives at row s of the [num_blocks*block_size]
+ *     x [num_kv_heads*head_dim] view.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). All work is
+ *     asynchronous on that stream: no host synchronisation, no allocation,
+ *     so every call can be captured in a CUDA graph.
+ *   - `status` (nullable) is a device int32. Kernels never trap; when they
+ *     meet an input they cannot honour (a slot or block id outside the cache,
+ *     a wait that timed out) they skip the offending access and OR a bit from
+ *     nvattn_status_bits into *status.
+ *   - Return value: NVATTN_OK, or an error code with a message available from
+ *     nvattn_last_error() (thread-local). Argument errors are detected on the
+ *     host before any launch.
+ */
+#ifndef NVATTN_H_
+#define NVATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NVATTN_API __attribute__((visibility("default")))
+#else
+#define NVATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nvattn_error {
+  NVATTN_OK = 0,
+  NVATTN_ERR_INVALID = 1,     /* bad argument: shape, stride, alignment, NULL */
+  NVATTN_ERR_UNSUPPORTED = 2, /* valid for the reference but not built here   */
+  NVATTN_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed            */
+  NVATTN_ERR_WORKSPACE = 4    /* caller-provided workspace too small          */
+};
+
+enum nvattn_status_bits {
+  NVATTN_STATUS_BAD_SLOT = 1,   /* slot_mapping entry outside [-1, num_slots)  */
+  NVATTN_STATUS_BAD_BLOCK = 2,  /* block_table entry outside [0, num_blocks)   */
+  NVATTN_STATUS_TIMEOUT = 4     /* a pipeline wait gave up (bounded spin)      */
+};
+
+/* Message of the last failed call on this host thread ("" if none). */
+NVATTN_API const char* nvattn_last_error(void);
+
+/* ABI version of this library: (major << 16) | minor. */
+NVATTN_API int nvattn_version(void);
+
+/*
+ * KV-cache scatter. Replaces store_kvcache (nanovllm/layers/attention.py:33-40)
+ * and its Triton kernel store_kvcache_kernel (attention.py:10-30):
+ *
+ *   for i in [0, num_tokens): if slot_mapping[i] != -1:
+ *     k_cache[slot_mapping[i]*D : +D] = key[i*key_stride : +D]
+ *     v_cache[slot_mapping[i]*D : +D] = value[i*value_stride : +D]
+ *
+ * D = num_kv_heads*head_dim elements (the reference asserts key.stride(1) ==
+ * head_dim, so a token's D elements are contiguous); key_stride/value_stride
+ * are the token strides (value is a strided view of the qkv projection in the
+ * engine). num_slots = num_blocks*block_size bounds the slot ids: entries
+ * outside [-1, num_slots) are skipped and flagged NVATTN_STATUS_BAD_SLOT.
+ * Bit-exact copy.
+ */
+NVATTN_API int nvattn_store_kvcache(const void* key, int64_t key_stride,
+                         const void* value, int64_t value_stride,
+                         void* k_cache, void* v_cache,
+                         const int32_t* slot_mapping, int64_t num_tokens,
+                         int64_t D, int64_t num_slots, int32_t* status,
+                         void* stream);
+
+/*
+ * Variable-length causal prefill. Replaces the call
+ *   flash_attn_varlen_func(q, k, v, max_seqlen_q, cu_seqlens_q, max_seqlen_k,
+ *                          cu_seqlens_k, softmax_scale, causal=True,
+ *                          block_table)
+ * at nanovllm/layers/attention.py:67-70.
+ *
+ *   q   [total_q][num_heads][head_dim]      strides (q_stride_tok, q_stride_head, 1)
+ *   out [total_q][num_heads][head_dim]      strides (o_stride_tok, o_stride_head, 1)
+ *   block_table == NULL (dense; attention.py:67 with block_tables None):
+ *     k, v [total_k][num_kv_heads][head_dim] strides (*_stride_tok, *_stride_head, 1)
+ *   block_table != NULL (prefix-cache hit; attention.py:65-66 swaps k,v for
+ *   the caches): k, v are the caches [num_blocks][block_size][num_kv_heads]
+ *     [head_dim] (contiguous; stride arguments ignored) and sequence b's key j
+ *     lives in block block_table[b*block_table_stride + j/block_size];
+ *     max_blocks_per_seq is the table width (keys beyond width*block_size are
+ *     ignored and flagged NVATTN_STATUS_BAD_BLOCK).
+ *
+ * cu_seqlens_q must stay within total_q rows (rows past it are not touched).
+ *
+ * Sequence b owns query rows [cu_seqlens_q[b], cu_seqlens_q[b+1]) and
+ * seqlen_k = cu_seqlens_k[b+1]-cu_seqlens_k[b] keys. With causal != 0 the mask
+ * is aligned to the bottom-right corner (flash-attn >= 2.1 semantics): query i
+ * of a sequence sees keys [0, seqlen_k - seqlen_q + i]; rows that see no key
+ * produce 0. Query head h reads KV head h / (num_heads/num_kv_heads).
+ * Scores and softmax are fp32; the output is rounded to bf16 once.
+ */
+NVATTN_API int nvattn_varlen_prefill(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                          const void* k, int64_t k_stride_tok, int64_t k_stride_head,
+                          const void* v, int64_t v_stride_tok, int64_t v_stride_head,
+                          void* out, int64_t o_stride_tok, int64_t o_stride_head,
+                          const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                          int32_t num_seqs, int32_t max_seqlen_q, int32_t max_seqlen_k,
+                          int64_t total_q, int64_t total_k,
+                          const int32_t* block_table, int64_t block_table_stride,
+                          int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
+                          int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                          float softmax_scale, int32_t causal,
+                          int32_t* status, void* stream);
+
+/*
+ * Paged decode (one query token per sequence). Replaces the call
+ *   flash_attn_with_kvcache(q.unsqueeze(1), k_cache, v_cache,
+ *                           cache_seqlens=context_lens, block_table=block_tables,
+ *                           softmax_scale, causal=True)
+ * at nanovllm/layers/attention.py:72-74.
+ *
+ *   q   [batch][num_heads][head_dim]   strides (q_stride_tok, q_stride_head, 1)
+ *   out [batch][num_heads][head_dim]   strides (o_stride_tok, o_stride_head, 1)
+ *   k_cache, v_cache [num_blocks][block_size][num_kv_heads][head_dim]
+ *   cache_seqlens[b] keys are read through block_table row b; a row with
+ *   cache_seqlens[b] == 0 (CUDA-graph padding, model_runner.py:206-209)
+ *   produces zeros. max_blocks_per_seq = block_table width; it fixes the
+ *   split-K grid, so the launch shape depends only on host-side sizes.
+ *
+ * Split-K partials go to `workspace` (device, >= nvattn_decode_workspace_bytes
+ * of the same sizes); the library allocates nothing.
+ */
+NVATTN_API size_t nvattn_decode_workspace_bytes(int32_t batch, int32_t num_heads, int32_t num_kv_heads,
+                                     int32_t max_blocks_per_seq, int32_t block_size);
+
+NVATTN_API int nvattn_paged_decode(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                        const void* k_cache, const void* v_cache,
+                        void* out, int64_t o_stride_tok, int64_t o_stride_head,
+                        const int32_t* cache_seqlens,
+                        const int32_t* block_table, int64_t block_table_stride,
+                        int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
+                        int32_t batch, int32_t num_heads, int32_t num_kv_heads,
+                        int32_t head_dim, float softmax_scale,
+                        void* workspace, size_t workspace_bytes,
+                        int32_t* status, void* stream);
+
+/*
+ * Tree-verification attention (no counterpart in the reference: EAGLE3-style
+ * speculative verification, new in this library).
+ *
+ * Sequence b has context_lens[b] committed tokens in the cache followed by
+ * n_b = cu_seqlens_q[b+1]-cu_seqlens_q[b] (<= 64) draft-tree nodes whose K/V
+ * were already scattered to cache positions context_lens[b] .. +n_b-1 (node i
+ * at position context_lens[b]+i, e.g. by nvattn_store_kvcache). Query row
+ * r = cu_seqlens_q[b]+j is node j; it attends every committed token and the
+ * tree nodes i whose bit i is set in tree_mask[r] (ancestors and itself).
+ * A chain mask (tree_mask[r] = 2^(j+1)-1) is ordinary causal prefill.
+ *
+ *   q, out [total_q][num_heads][head_dim]; caches and block_table as in
+ *   nvattn_varlen_prefill's paged mode; tree_mask [total_q] uint64.
+ */
+NVATTN_API int nvattn_tree_verify(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                       const void* k_cache, const void* v_cache,
+                       void* out, int64_t o_stride_tok, int64_t o_stride_head,
+                       const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                       const uint64_t* tree_mask,
+                       const int32_t* block_table, int64_t block_table_stride,
+                       int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
+                       int32_t num_seqs, int32_t max_nodes, int64_t total_q,
+                       int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
+                       float softmax_scale, int32_t* status, void* stream);
+
+/*
+ * In-cache slot moves, grouped (no counterpart in the reference: compaction
+ * of an accepted speculative path). Group g moves rows
+ *   src_slots[i] -> dst_slots[i], i in [cu_moves[g], cu_moves[g+1])
+ * of both caches (row = D contiguous elements). Every source row of a group is
+ * read before any destination row of that group is written, so a group may
+ * shift rows onto positions its own sources occupy; different groups must
+ * touch disjoint slots. At most 64 moves per group; num_moves is the length of
+ * src_slots/dst_slots (group bounds past it are clamped and flagged).
+ */
+NVATTN_API int nvattn_kv_move(void* k_cache, void* v_cache,
+                   const int32_t* src_slots, const int32_t* dst_slots,
+                   const int32_t* cu_moves, int32_t num_groups, int32_t num_moves,
+                   int64_t D, int64_t num_slots, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* NVATTN_H_ */

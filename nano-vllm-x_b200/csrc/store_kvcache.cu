@@ -1,0 +1,208 @@
+// KV-cache scatter (replaces store_kvcache / store_kvcache_kernel,
+// nanovllm/layers/attention.py:10-40) and grouped in-cache slot moves.
+//
+// The reference runs one Triton program per token that loads D elements of K
+// and V and stores them at slot*D. Here one warp owns one token: its 32 lanes
+// move the K row then the V row in VEC-byte vectors (16 bytes when every
+// pointer, stride and D allow it), so each warp instruction touches 512
+// contiguous bytes on both the load and the store side. A CTA of 8 warps
+// covers 8 tokens; the grid is ceil(N/8) CTAs. Pure copy: bit-exact.
+#include "common.cuh"
+
+namespace nvattn {
+
+template <int VEC>
+struct VecType;
+template <>
+struct VecType<16> {
+  using T = int4;
+};
+template <>
+struct VecType<8> {
+  using T = int2;
+};
+template <>
+struct VecType<4> {
+  using T = int;
+};
+template <>
+struct VecType<2> {
+  using T = short;
+};
+
+constexpr int kStoreWarps = 8;
+
+template <int VEC>
+__global__ void __launch_bounds__(kStoreWarps * 32)
+    store_kvcache_kernel(const char* __restrict__ key, int64_t key_stride_b,
+                         const char* __restrict__ value, int64_t value_stride_b,
+                         char* __restrict__ k_cache, char* __restrict__ v_cache,
+                         const int32_t* __restrict__ slot_mapping, int64_t n_tokens,
+                         int64_t row_bytes, int64_t num_slots, int32_t* status) {
+  using V = typename VecType<VEC>::T;
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = static_cast<int64_t>(blockIdx.x) * kStoreWarps + (threadIdx.x >> 5);
+  if (tok >= n_tokens) return;
+  const int64_t slot = slot_mapping[tok];
+  if (slot == -1) return;  // attention.py:23
+  if (slot < 0 || slot >= num_slots) {
+    if (lane == 0) set_status(status, NVATTN_STATUS_BAD_SLOT);
+    return;
+  }
+  const int64_t nvec = row_bytes / VEC;
+  const V* ksrc = reinterpret_cast<const V*>(key + tok * key_stride_b);
+  const V* vsrc = reinterpret_cast<const V*>(value + tok * value_stride_b);
+  V* kdst = reinterpret_cast<V*>(k_cache + slot * row_bytes);
+  V* vdst = reinterpret_cast<V*>(v_cache + slot * row_bytes);
+  // Issue all loads of this lane before its stores so the two rows' reads
+  // overlap in flight.
+  for (int64_t i = lane; i < nvec; i += 64) {
+    V k0 = __ldg(ksrc + i);
+    V v0 = __ldg(vsrc + i);
+    const bool two = i + 32 < nvec;
+    V k1, v1;
+    if (two) {
+      k1 = __ldg(ksrc + i + 32);
+      v1 = __ldg(vsrc + i + 32);
+    }
+    kdst[i] = k0;
+    vdst[i] = v0;
+    if (two) {
+      kdst[i + 32] = k1;
+      vdst[i + 32] = v1;
+    }
+  }
+}
+
+// Group g: read every source row of the group into shared memory, then write
+// all destinations, so a group may shift rows onto its own sources. Rows are
+// processed in column chunks of kMoveChunk bytes; chunks of different columns
+// never overlap, so read-all-then-write per chunk keeps the guarantee.
+constexpr int kMoveMax = 64;
+constexpr int kMoveChunk = 128;  // 2 x 64 x 128 B = 16 KB of static shared memory
+
+__global__ void __launch_bounds__(256)
+    kv_move_kernel(char* __restrict__ k_cache, char* __restrict__ v_cache,
+                   const int32_t* __restrict__ src, const int32_t* __restrict__ dst,
+                   const int32_t* __restrict__ cu_moves, int32_t num_moves, int64_t row_bytes,
+                   int64_t num_slots, int32_t* status) {
+  __shared__ int4 kbuf[kMoveMax * kMoveChunk / 16];
+  __shared__ int4 vbuf[kMoveMax * kMoveChunk / 16];
+  const int g = blockIdx.x;
+  const int begin = cu_moves[g];
+  int end = cu_moves[g + 1];
+  if (begin < 0 || end > num_moves) {
+    if (threadIdx.x == 0) set_status(status, NVATTN_STATUS_BAD_SLOT);
+    end = min(end, num_moves);
+  }
+  int count = end - begin;
+  if (begin < 0 || count <= 0) return;
+  if (count > kMoveMax) {
+    if (threadIdx.x == 0) set_status(status, NVATTN_STATUS_BAD_SLOT);
+    count = kMoveMax;
+  }
+  for (int64_t col = 0; col < row_bytes; col += kMoveChunk) {
+    const int64_t width = (row_bytes - col < kMoveChunk) ? row_bytes - col : kMoveChunk;
+    const int nvec = static_cast<int>(width / 16);
+    for (int e = threadIdx.x; e < count * nvec; e += blockDim.x) {
+      const int m = e / nvec, i = e % nvec;
+      const int64_t s = src[begin + m];
+      int4 kv = make_int4(0, 0, 0, 0), vv = make_int4(0, 0, 0, 0);
+      if (s >= 0 && s < num_slots) {
+        kv = reinterpret_cast<const int4*>(k_cache + s * row_bytes + col)[i];
+        vv = reinterpret_cast<const int4*>(v_cache + s * row_bytes + col)[i];
+      }
+      kbuf[m * nvec + i] = kv;
+      vbuf[m * nvec + i] = vv;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < count * nvec; e += blockDim.x) {
+      const int m = e / nvec, i = e % nvec;
+      const int64_t s = src[begin + m];
+      const int64_t d = dst[begin + m];
+      if (s < 0 || s >= num_slots || d < 0 || d >= num_slots) {
+        if (i == 0 && col == 0) set_status(status, NVATTN_STATUS_BAD_SLOT);
+        continue;
+      }
+      reinterpret_cast<int4*>(k_cache + d * row_bytes + col)[i] = kbuf[m * nvec + i];
+      reinterpret_cast<int4*>(v_cache + d * row_bytes + col)[i] = vbuf[m * nvec + i];
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace nvattn
+
+using namespace nvattn;
+
+extern "C" int nvattn_store_kvcache(const void* key, int64_t key_stride, const void* value,
+                                    int64_t value_stride, void* k_cache, void* v_cache,
+                                    const int32_t* slot_mapping, int64_t num_tokens, int64_t D,
+                                    int64_t num_slots, int32_t* status, void* stream) {
+  clear_error();
+  if (num_tokens < 0 || D <= 0 || num_slots < 0)
+    return fail(NVATTN_ERR_INVALID, "store_kvcache: negative size");
+  if (num_tokens == 0) return NVATTN_OK;
+  if (!key || !value || !k_cache || !v_cache || !slot_mapping)
+    return fail(NVATTN_ERR_INVALID, "store_kvcache: NULL pointer");
+  if (key_stride < D || value_stride < D)
+    return fail(NVATTN_ERR_INVALID, "store_kvcache: token stride smaller than D (rows overlap)");
+  const int64_t row_bytes = D * 2;
+  // Widest vector that every address and stride allows.
+  auto fits = [&](int v) {
+    return (row_bytes % v == 0) && ((key_stride * 2) % v == 0) && ((value_stride * 2) % v == 0) &&
+           (reinterpret_cast<uintptr_t>(key) % v == 0) &&
+           (reinterpret_cast<uintptr_t>(value) % v == 0) &&
+           (reinterpret_cast<uintptr_t>(k_cache) % v == 0) &&
+           (reinterpret_cast<uintptr_t>(v_cache) % v == 0);
+  };
+  const int64_t blocks = (num_tokens + kStoreWarps - 1) / kStoreWarps;
+  if (blocks > 0x7fffffff) return fail(NVATTN_ERR_INVALID, "store_kvcache: too many tokens");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  dim3 grid(static_cast<unsigned>(blocks)), block(kStoreWarps * 32);
+  const char* kp = static_cast<const char*>(key);
+  const char* vp = static_cast<const char*>(value);
+  char* kc = static_cast<char*>(k_cache);
+  char* vc = static_cast<char*>(v_cache);
+  if (fits(16))
+    store_kvcache_kernel<16><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
+                                                    vc, slot_mapping, num_tokens, row_bytes,
+                                                    num_slots, status);
+  else if (fits(8))
+    store_kvcache_kernel<8><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
+                                                   vc, slot_mapping, num_tokens, row_bytes,
+                                                   num_slots, status);
+  else if (fits(4))
+    store_kvcache_kernel<4><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
+                                                   vc, slot_mapping, num_tokens, row_bytes,
+                                                   num_slots, status);
+  else
+    store_kvcache_kernel<2><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
+                                                   vc, slot_mapping, num_tokens, row_bytes,
+                                                   num_slots, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "store_kvcache launch");
+  return NVATTN_OK;
+}
+
+extern "C" int nvattn_kv_move(void* k_cache, void* v_cache, const int32_t* src_slots,
+                              const int32_t* dst_slots, const int32_t* cu_moves,
+                              int32_t num_groups, int32_t num_moves, int64_t D,
+                              int64_t num_slots, int32_t* status, void* stream) {
+  clear_error();
+  if (num_groups < 0 || num_moves < 0 || D <= 0)
+    return fail(NVATTN_ERR_INVALID, "kv_move: bad sizes");
+  if (num_groups == 0) return NVATTN_OK;
+  if (!k_cache || !v_cache || !src_slots || !dst_slots || !cu_moves)
+    return fail(NVATTN_ERR_INVALID, "kv_move: NULL pointer");
+  const int64_t row_bytes = D * 2;
+  if (row_bytes % 16 || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(NVATTN_ERR_UNSUPPORTED, "kv_move: rows must be 16-byte multiples and aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  kv_move_kernel<<<num_groups, 256, 0, s>>>(static_cast<char*>(k_cache),
+                                               static_cast<char*>(v_cache), src_slots, dst_slots,
+                                               cu_moves, num_moves, row_bytes, num_slots, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "kv_move launch");
+  return NVATTN_OK;
+}

@@ -1,0 +1,25 @@
+"""nvattn — B200 (sm_100a) paged-KV attention for Nano-vLLM-X.
+
+Drop-in for nanovllm/layers/attention.py: ``Attention`` (same constructor and
+``forward(q, k, v)``), the context module mirror, and the operators that
+replace the reference's Triton scatter and flash-attn calls. Kernels live in
+the in-tree ``libnvattn.so`` (C ABI: include/nvattn.h); build it with
+``python -m nvattn.build``.
+"""
+from .attention import Attention
+from .context import Context, get_context, reset_context, set_context
+from . import ops, tree, parallel
+from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, kv_move, paged_decode,
+                  store_kvcache, tree_attention, varlen_prefill)
+
+__all__ = [
+    "Attention", "Context", "get_context", "set_context", "reset_context", "ops", "tree",
+    "parallel", "store_kvcache", "varlen_prefill", "paged_decode", "tree_attention", "kv_move",
+    "flash_attn_varlen_func", "flash_attn_with_kvcache", "install",
+]
+
+
+def install() -> None:
+    """Replace Nano-vLLM-X's Attention with nvattn's (see nvattn.install)."""
+    from .install import install as _install
+    _install()

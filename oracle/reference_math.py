@@ -1,0 +1,230 @@
+"""CPU oracle for the attention path — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline arm may
+import this module, and only as the checker (or as the timed CPU baseline).
+The product path (nvattn) never calls it.
+
+It restates, on the CPU, what the reference computes on the path that nvattn
+replaces (nanovllm/layers/attention.py):
+
+* ``store_kvcache``       — the Triton scatter store_kvcache_kernel
+  (attention.py:10-30) and its wrapper's contract (attention.py:33-40);
+  numpy index copy, bit-exact.
+* ``varlen_attention``    — flash_attn_varlen_func as called at
+  attention.py:67-70. flash-attn is a third-party dependency (unpinned in the
+  reference's pyproject.toml:18; 2.8.3 in this image). Its published
+  semantics are restated: softmax(scale * Q K^T + mask) V per sequence of
+  the varlen batch, causal mask aligned to the bottom-right corner (query i
+  of a sequence sees keys j <= seqlen_k - seqlen_q + i), GQA head map
+  h -> h // (H / KVH), rows with no visible key output 0, and in paged mode
+  (block_table given, attention.py:65-66) key j of sequence b is row
+  j % block_size of block block_table[b, j // block_size].
+* ``decode_attention``    — flash_attn_with_kvcache at attention.py:72-74:
+  one query per sequence over cache_seqlens[b] cached keys (causal is moot
+  for a single query); cache_seqlens == 0 gives 0.
+* ``tree_attention``      — no reference code: the ancestor-mask definition
+  (a node sees the whole committed context plus the tree nodes whose bits
+  are set in its mask word).
+* ``kv_move``             — grouped in-cache moves, read-all-then-write.
+
+All attention math is float32 on torch CPU tensors (inputs are bf16); the
+result is float32 so tests can state their tolerance against it.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+
+# ---------------------------------------------------------------- KV scatter
+
+def store_kvcache(key: np.ndarray, value: np.ndarray, k_cache: np.ndarray,
+                  v_cache: np.ndarray, slot_mapping: np.ndarray) -> None:
+    """In place: k_cache.reshape(-1, D)[slot] = key.reshape(N, D)[i] for slot != -1.
+
+    Follows store_kvcache_kernel (nanovllm/layers/attention.py:20-30): token i
+    reads D contiguous elements at i*key_stride (numpy strides carry that) and
+    writes them at slot*D; slot == -1 skips the token (attention.py:23).
+    Arrays are raw 16-bit patterns (np.uint16) so the copy is bit-exact.
+    """
+    n = key.shape[0]
+    D = int(np.prod(key.shape[1:]))
+    kc = k_cache.reshape(-1, D)
+    vc = v_cache.reshape(-1, D)
+    slots = np.asarray(slot_mapping).astype(np.int64)
+    assert slots.shape == (n,)
+    keep = slots != -1
+    kc[slots[keep]] = key.reshape(n, D)[keep]
+    vc[slots[keep]] = value.reshape(n, D)[keep]
+
+
+def kv_move(k_cache: np.ndarray, v_cache: np.ndarray, src: np.ndarray, dst: np.ndarray,
+            cu_moves: np.ndarray) -> None:
+    """Grouped moves: every source row of a group is read before any write."""
+    D = k_cache.shape[-2] * k_cache.shape[-1]
+    kc = k_cache.reshape(-1, D)
+    vc = v_cache.reshape(-1, D)
+    for g in range(len(cu_moves) - 1):
+        a, b = int(cu_moves[g]), int(cu_moves[g + 1])
+        s = np.asarray(src[a:b], dtype=np.int64)
+        d = np.asarray(dst[a:b], dtype=np.int64)
+        krows, vrows = kc[s].copy(), vc[s].copy()
+        kc[d] = krows
+        vc[d] = vrows
+
+
+# ----------------------------------------------------------------- attention
+
+def gather_paged(cache: torch.Tensor, block_row, n: int) -> torch.Tensor:
+    """Keys 0..n-1 of one sequence from a (num_blocks, block_size, KVH, d) cache."""
+    bs = cache.shape[1]
+    nblk = (n + bs - 1) // bs
+    blocks = torch.as_tensor(np.asarray(block_row[:nblk], dtype=np.int64))
+    return cache[blocks].reshape(nblk * bs, *cache.shape[2:])[:n]
+
+
+def _attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+            allowed: torch.Tensor | None) -> torch.Tensor:
+    """q (Lq, H, d), k/v (Lk, KVH, d), allowed (Lq, Lk) bool or None -> (Lq, H, d) fp32."""
+    Lq, H, d = q.shape
+    Lk, KVH, _ = k.shape
+    group = H // KVH
+    qf = q.float().reshape(Lq, KVH, group, d).permute(1, 2, 0, 3)  # (KVH, g, Lq, d)
+    kf = k.float().permute(1, 0, 2)                                # (KVH, Lk, d)
+    vf = v.float().permute(1, 0, 2)
+    s = torch.einsum("hgqd,hkd->hgqk", qf, kf) * scale
+    if allowed is not None:
+        s = s.masked_fill(~allowed.view(1, 1, Lq, Lk), float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    p = torch.nan_to_num(p, nan=0.0)  # rows with no visible key -> 0
+    o = torch.einsum("hgqk,hkd->hgqd", p, vf)                      # (KVH, g, Lq, d)
+    return o.permute(2, 0, 1, 3).reshape(Lq, H, d)
+
+
+def causal_allowed(Lq: int, Lk: int) -> torch.Tensor:
+    """Bottom-right aligned causal mask: query i sees keys j <= Lk - Lq + i."""
+    i = torch.arange(Lq).view(-1, 1)
+    j = torch.arange(Lk).view(1, -1)
+    return j <= (Lk - Lq) + i
+
+
+def varlen_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     cu_seqlens_q, cu_seqlens_k, scale: float, causal: bool = True,
+                     block_table=None) -> torch.Tensor:
+    """flash_attn_varlen_func semantics (attention.py:67-70); returns fp32 (total_q, H, d)."""
+    cu_q = np.asarray(cu_seqlens_q, dtype=np.int64)
+    cu_k = np.asarray(cu_seqlens_k, dtype=np.int64)
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    for b in range(len(cu_q) - 1):
+        qs, qe = int(cu_q[b]), int(cu_q[b + 1])
+        Lq = qe - qs
+        Lk = int(cu_k[b + 1] - cu_k[b])
+        if Lq == 0:
+            continue
+        if block_table is not None:
+            kb = gather_paged(k, block_table[b], Lk)
+            vb = gather_paged(v, block_table[b], Lk)
+        else:
+            kb = k[int(cu_k[b]):int(cu_k[b + 1])]
+            vb = v[int(cu_k[b]):int(cu_k[b + 1])]
+        allowed = causal_allowed(Lq, Lk) if causal else None
+        out[qs:qe] = _attend(q[qs:qe], kb, vb, scale, allowed)
+    return out
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     cache_seqlens, block_table, scale: float) -> torch.Tensor:
+    """flash_attn_with_kvcache for one query per sequence (attention.py:72-74).
+
+    q (B, H, d) -> fp32 (B, H, d).
+    """
+    lens = np.asarray(cache_seqlens, dtype=np.int64)
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    for b in range(q.shape[0]):
+        n = int(lens[b])
+        if n == 0:
+            continue
+        kb = gather_paged(k_cache, block_table[b], n)
+        vb = gather_paged(v_cache, block_table[b], n)
+        out[b:b + 1] = _attend(q[b:b + 1], kb, vb, scale, None)
+    return out
+
+
+def tree_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                   cu_seqlens_q, context_lens, tree_mask, block_table,
+                   scale: float) -> torch.Tensor:
+    """Ancestor-mask attention: node j of sequence b sees cache keys [0, ctx_b)
+    and tree node i (cache position ctx_b + i) iff bit i of tree_mask[row j]."""
+    cu_q = np.asarray(cu_seqlens_q, dtype=np.int64)
+    ctx = np.asarray(context_lens, dtype=np.int64)
+    masks = np.asarray(tree_mask).astype(np.uint64)
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    for b in range(len(cu_q) - 1):
+        qs, qe = int(cu_q[b]), int(cu_q[b + 1])
+        n = qe - qs
+        if n == 0:
+            continue
+        c = int(ctx[b])
+        kb = gather_paged(k_cache, block_table[b], c + n)
+        vb = gather_paged(v_cache, block_table[b], c + n)
+        allowed = torch.ones(n, c + n, dtype=torch.bool)
+        for j in range(n):
+            w = int(masks[qs + j])
+            allowed[j, c:] = torch.tensor([(w >> i) & 1 == 1 for i in range(n)])
+        out[qs:qe] = _attend(q[qs:qe], kb, vb, scale, allowed)
+    return out
+
+
+# ------------------------------------------------------ engine-side metadata
+
+def prepare_prefill_metadata(seqs, block_size: int):
+    """Restates ModelRunner.prepare_prefill (model_runner.py:129-170).
+
+    seqs: list of dicts with ``num_tokens`` (tokens scheduled end), ``start``
+    (= num_cached_tokens), ``num_scheduled`` and ``block_table`` (list).
+    Returns (cu_seqlens_q, cu_seqlens_k, max_q, max_k, slot_mapping,
+    block_tables or None) as numpy int32 / ints.
+    """
+    cu_q, cu_k = [0], [0]
+    max_q = max_k = 0
+    slots = []
+    for s in seqs:
+        start = s["start"]
+        seqlen_q = s["num_scheduled"]
+        end = start + seqlen_q
+        cu_q.append(cu_q[-1] + seqlen_q)
+        cu_k.append(cu_k[-1] + end)
+        max_q = max(max_q, seqlen_q)
+        max_k = max(max_k, end)
+        bt = s["block_table"]
+        if not bt:
+            continue
+        for pos in range(start, end):
+            slots.append(bt[pos // block_size] * block_size + pos % block_size)
+    tables = None
+    if cu_k[-1] > cu_q[-1]:  # prefix cache (model_runner.py:162-163)
+        tables = padded_block_tables([s["block_table"] for s in seqs])
+    return (np.array(cu_q, np.int32), np.array(cu_k, np.int32), max_q, max_k,
+            np.array(slots, np.int32), tables)
+
+
+def prepare_decode_metadata(seqs, block_size: int):
+    """Restates ModelRunner.prepare_decode (model_runner.py:172-188).
+
+    seqs: dicts with ``num_tokens`` (len(seq), the new token included) and
+    ``block_table``. Returns (slot_mapping, context_lens, block_tables).
+    """
+    slots, lens = [], []
+    for s in seqs:
+        n = s["num_tokens"]
+        last_block_tokens = n - (len(s["block_table"]) - 1) * block_size
+        slots.append(s["block_table"][-1] * block_size + last_block_tokens - 1)
+        lens.append(n)
+    tables = padded_block_tables([s["block_table"] for s in seqs])
+    return np.array(slots, np.int32), np.array(lens, np.int32), tables
+
+
+def padded_block_tables(tables):
+    """model_runner.py:123-127: pad rows with -1 to the longest table."""
+    width = max(len(t) for t in tables)
+    return np.array([list(t) + [-1] * (width - len(t)) for t in tables], dtype=np.int32)

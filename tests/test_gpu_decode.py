@@ -1,0 +1,145 @@
+"""Paged split-K decode on the GPU against the oracle (max-abs 1e-2, bf16 out
+vs fp32 reference)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import max_err, paged_layout, random_cache
+from oracle import reference_math as R
+
+from nvattn import ops
+
+pytestmark = pytest.mark.gpu
+dev = torch.device("cuda")
+TOL = 1e-2
+
+
+def _run(lens, H, KVH, block_size=256, seed=0, extra_width=0, nan_fill=False):
+    g = torch.Generator().manual_seed(seed)
+    nblocks, bt = paged_layout(lens, block_size, seed=seed)
+    if extra_width:  # block_table wider than needed (CUDA-graph static buffer)
+        bt = torch.cat([bt, torch.full((len(lens), extra_width), -1, dtype=torch.int32)], 1)
+    kc = random_cache(nblocks, block_size, KVH, g)
+    vc = random_cache(nblocks, block_size, KVH, g)
+    if nan_fill:
+        # stale bytes past each context end: NaN must not leak into the output
+        for b, n in enumerate(lens):
+            for j in range(int(n), ((int(n) + block_size - 1) // block_size) * block_size):
+                blk = int(bt[b, j // block_size])
+                kc[blk, j % block_size] = float("nan")
+                vc[blk, j % block_size] = float("nan")
+    q = torch.randn(len(lens), H, 128, generator=g).to(torch.bfloat16)
+    seqlens = torch.tensor(lens, dtype=torch.int32)
+    out = ops.paged_decode(q.to(dev), kc.to(dev), vc.to(dev), seqlens.to(dev), bt.to(dev),
+                           softmax_scale=128 ** -0.5)
+    torch.cuda.synchronize()
+    ref = R.decode_attention(q, kc, vc, seqlens.numpy(), bt.numpy(), 128 ** -0.5)
+    return out, ref
+
+
+@pytest.mark.parametrize("H,KVH", [(64, 8), (16, 8), (32, 8), (8, 1), (16, 1), (4, 4)])
+def test_group_sizes(H, KVH):
+    rng = np.random.default_rng(H + KVH)
+    lens = rng.integers(1, 3000, size=6).tolist()
+    out, ref = _run(lens, H, KVH, seed=H)
+    assert max_err(out, ref) < TOL
+    assert ops.read_status() == 0
+
+
+def test_block_boundary_lengths():
+    lens = [1, 2, 63, 64, 65, 127, 128, 255, 256, 257, 511, 512, 513, 2047, 2048, 2049, 4097]
+    out, ref = _run(lens, 32, 8, seed=3)
+    assert max_err(out, ref) < TOL
+
+
+def test_zero_length_rows_give_zeros():
+    # CUDA-graph padding rows: context_lens 0, stale block-table rows
+    lens = [0, 300, 0, 5]
+    out, ref = _run(lens, 16, 8, seed=4)
+    assert torch.all(out[0] == 0) and torch.all(out[2] == 0)
+    assert max_err(out, ref) < TOL
+
+
+def test_stale_nan_past_context_end_is_ignored():
+    out, ref = _run([5, 70, 300], 16, 8, seed=5, nan_fill=True)
+    assert torch.isfinite(out.float()).all()
+    assert max_err(out, ref) < TOL
+
+
+def test_single_split_path():
+    # enough (sequence, kv-head) pairs that one split per pair is chosen
+    rng = np.random.default_rng(9)
+    lens = rng.integers(1, 2048, size=300).tolist()
+    assert ops.decode_workspace_bytes(300, 16, 8, 8, 256) == 0
+    out, ref = _run(lens, 16, 8, seed=9)
+    assert max_err(out, ref) < TOL
+
+
+def test_long_context_qwen3_32b_shape():
+    # cfg4 shape at reduced batch: 64Q/8KV heads, contexts into the tens of thousands
+    rng = np.random.default_rng(11)
+    lens = rng.integers(4096, 32768, size=3).tolist()
+    out, ref = _run(lens, 64, 8, seed=11)
+    assert max_err(out, ref) < TOL
+
+
+def test_block_size_512():
+    out, ref = _run([100, 600, 1500], 16, 8, block_size=512, seed=12)
+    assert max_err(out, ref) < TOL
+
+
+def test_wide_block_table_and_graph_capture():
+    """Capture decode in a CUDA graph on static buffers, replay with new metadata."""
+    g = torch.Generator().manual_seed(13)
+    H, KVH, bs, width, B = 16, 8, 256, 16, 8
+    nblocks = B * width
+    kc = random_cache(nblocks, bs, KVH, g).to(dev)
+    vc = random_cache(nblocks, bs, KVH, g).to(dev)
+    q = torch.zeros(B, H, 128, dtype=torch.bfloat16, device=dev)
+    lens = torch.zeros(B, dtype=torch.int32, device=dev)
+    bt = torch.zeros(B, width, dtype=torch.int32, device=dev)
+    out = torch.empty(B, H, 128, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(max(1, ops.decode_workspace_bytes(B, H, KVH, width, bs)), dtype=torch.uint8,
+                     device=dev)
+    ops.status_tensor()  # created before capture
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ops.paged_decode(q, kc, vc, lens, bt, out=out, workspace=ws)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.paged_decode(q, kc, vc, lens, bt, out=out, workspace=ws)
+    for trial in range(3):
+        rng = np.random.default_rng(100 + trial)
+        new_lens = rng.integers(0, width * bs, size=B).astype(np.int32)
+        perm = rng.permutation(nblocks)[:B * width].reshape(B, width).astype(np.int32)
+        qn = torch.randn(B, H, 128, generator=g).to(torch.bfloat16)
+        q.copy_(qn.to(dev))
+        lens.copy_(torch.from_numpy(new_lens).to(dev))
+        bt.copy_(torch.from_numpy(perm).to(dev))
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = R.decode_attention(qn, kc.cpu(), vc.cpu(), new_lens, perm, 128 ** -0.5)
+        assert max_err(out, ref) < TOL
+    assert ops.read_status() == 0
+
+
+def test_flash_attn_with_kvcache_signature():
+    """The keyword form used at attention.py:72-74 returns (B, 1, H, d)."""
+    g = torch.Generator().manual_seed(14)
+    lens = [10, 400]
+    nblocks, bt = paged_layout(lens, 256, seed=14)
+    kc = random_cache(nblocks, 256, 2, g)
+    vc = random_cache(nblocks, 256, 2, g)
+    q = torch.randn(2, 8, 128, generator=g).to(torch.bfloat16)
+    o = ops.flash_attn_with_kvcache(q.to(dev).unsqueeze(1), kc.to(dev), vc.to(dev),
+                                    cache_seqlens=torch.tensor(lens, dtype=torch.int32,
+                                                               device=dev),
+                                    block_table=bt.to(dev), softmax_scale=128 ** -0.5,
+                                    causal=True)
+    assert o.shape == (2, 1, 8, 128)
+    ref = R.decode_attention(q, kc, vc, np.array(lens), bt.numpy(), 128 ** -0.5)
+    assert max_err(o[:, 0], ref) < TOL

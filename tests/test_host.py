@@ -1,0 +1,147 @@
+"""Host-side checks that need no GPU: the C ABI library, argument validation,
+tree bookkeeping and head sharding."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import REPO
+
+import nvattn
+from nvattn import _lib, ops, parallel, tree
+
+
+def _header_symbols():
+    text = (REPO / "include" / "nvattn.h").read_text()
+    return sorted(set(re.findall(r"NVATTN_API\s+[\w\s\*]+?\b(nvattn_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    lib = _lib.load()
+    names = _header_symbols()
+    assert len(names) >= 8
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    assert _lib.version()[0] == 1
+
+
+def test_c_abi_rejects_bad_arguments_before_any_launch():
+    lib = _lib.load()
+    # NULL pointers with work to do -> NVATTN_ERR_INVALID, message set
+    rc = lib.nvattn_store_kvcache(None, 128, None, 128, None, None, None, 4, 128, 256, None, None)
+    assert rc == _lib.ERR_INVALID
+    assert b"NULL" in lib.nvattn_last_error()
+    # nothing to do -> OK without touching the device
+    assert lib.nvattn_store_kvcache(None, 0, None, 0, None, None, None, 0, 128, 0, None,
+                                    None) == _lib.OK
+    # unsupported head_dim / group sizes
+    fake = ctypes.c_void_p(0x1000)
+    rc = lib.nvattn_paged_decode(fake, 256, 64, fake, fake, fake, 256, 64, fake, fake, 4, 4,
+                                 8, 256, 2, 4, 2, 64, ctypes.c_float(0.1), None, 0, None, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"head_dim" in lib.nvattn_last_error()
+    rc = lib.nvattn_paged_decode(fake, 256, 128, fake, fake, fake, 256, 128, fake, fake, 4, 4,
+                                 8, 256, 2, 64, 2, 128, ctypes.c_float(0.1), None, 0, None, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"16 query heads" in lib.nvattn_last_error()
+    rc = lib.nvattn_paged_decode(fake, 256, 128, fake, fake, fake, 256, 128, fake, fake, 4, 4,
+                                 8, 100, 2, 4, 2, 128, ctypes.c_float(0.1), None, 0, None, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"block_size" in lib.nvattn_last_error()
+    rc = lib.nvattn_tree_verify(fake, 256, 128, fake, fake, fake, 256, 128, fake, fake, fake,
+                                fake, 4, 4, 8, 256, 1, 65, 65, 4, 1, 128, ctypes.c_float(0.1),
+                                None, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"64 tree nodes" in lib.nvattn_last_error()
+    rc = lib.nvattn_kv_move(None, None, None, None, None, 2, 4, 256, 100, None, None)
+    assert rc == _lib.ERR_INVALID
+
+
+def test_python_wrapper_raises_through_error_path():
+    with pytest.raises(_lib.NvattnError) as ei:
+        _lib.call("nvattn_kv_move", None, None, None, None, None, 1, 2, 256, 10, None, None)
+    assert ei.value.code == _lib.ERR_INVALID
+
+
+def test_ops_refuse_cpu_tensors_no_fallback():
+    k = torch.zeros(2, 1, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(1, 256, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.store_kvcache(k, k, kc, kc, torch.zeros(2, dtype=torch.int32))
+    q = torch.zeros(2, 4, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.paged_decode(q, kc, kc, torch.ones(2, dtype=torch.int32),
+                         torch.zeros(2, 1, dtype=torch.int32))
+
+
+def test_store_kvcache_keeps_reference_assertions():
+    # reference asserts (attention.py:36-39) fire before the device check
+    k = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    kc = torch.zeros(1, 256, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):
+        ops.store_kvcache(k, k, kc, kc, torch.zeros(3, dtype=torch.int32))
+    with pytest.raises(AssertionError):
+        ops.store_kvcache(k.transpose(0, 1).contiguous().transpose(0, 1), k, kc, kc,
+                          torch.zeros(4, dtype=torch.int32))
+
+
+def test_decode_workspace_size_is_deterministic():
+    a = ops.decode_workspace_bytes(128, 64, 8, 128, 256)
+    b = ops.decode_workspace_bytes(128, 64, 8, 128, 256)
+    assert a == b and a > 0
+    # one short sequence batch needs no split-K partials beyond one split
+    assert ops.decode_workspace_bytes(1, 8, 8, 1, 256) >= 0
+
+
+def test_draft_tree_shape_and_masks():
+    parents, depths = tree.build_draft_tree((4, 3, 2, 1, 1, 1), 64)
+    assert len(parents) == 64 and parents[0] == -1
+    assert depths.max() == 6
+    assert all(parents[j] < j for j in range(1, 64))
+    # per-level fan-out never exceeds the branching factor
+    for j in range(64):
+        kids = int((parents == j).sum())
+        assert kids <= (4, 3, 2, 1, 1, 1, 0)[depths[j]]
+    m = tree.ancestor_masks(parents)
+    for j in range(64):
+        bits = [i for i in range(64) if (int(m[j]) >> i) & 1]
+        chain, x = [], j
+        while x >= 0:
+            chain.append(x)
+            x = int(parents[x])
+        assert sorted(chain) == bits
+    assert tree.chain_masks(3).tolist() == [1, 3, 7]
+
+
+def test_greedy_accept_and_compaction_moves():
+    parents, _ = tree.build_draft_tree((2, 2), 7)
+    tokens = np.array([0, 10, 11, 20, 21, 22, 23])
+    # root predicts 11 -> node 2; node 2 predicts 23 -> its child with token 23
+    argmax = np.array([11, 0, 23, 0, 0, 0, 0])
+    path = tree.greedy_accept(parents, tokens, argmax)
+    assert path[0] == 0 and tokens[path[1]] == 11 and tokens[path[2]] == 23
+    src, dst = tree.compaction_moves(300, path, [7, 3], 256)
+    assert dst[0] == 3 * 256 + (301 - 256)
+    assert len(src) == len(dst) == 2
+
+
+def test_ngram_draft():
+    toks = [5, 6, 7, 8, 1, 2, 5, 6, 7]
+    assert tree.ngram_draft(toks, 3) == [8, 1, 2]
+    assert tree.ngram_draft([1, 2, 3], 4) == []
+
+
+def test_head_shard_matches_engine_split():
+    assert parallel.head_shard(64, 8, 7, 8) == ((56, 64), (7, 8))
+    assert parallel.head_shard(16, 8, 1, 2) == ((8, 16), (4, 8))
+    with pytest.raises(ValueError):
+        parallel.head_shard(16, 8, 0, 3)
+
+
+def test_package_surface():
+    for name in ("Attention", "store_kvcache", "flash_attn_varlen_func",
+                 "flash_attn_with_kvcache", "tree_attention", "kv_move", "install"):
+        assert hasattr(nvattn, name)
+    a = nvattn.Attention(16, 128, 128 ** -0.5, 8)
+    assert a.k_cache.numel() == 0 and hasattr(a, "v_cache")

@@ -1,0 +1,142 @@
+"""The CPU oracle pinned against the reference (golden fixtures), CPU only."""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, from_bits
+from oracle import reference_math as R
+from cases import CASES, make_case
+
+
+def test_store_kvcache_matches_reference_triton_kernel():
+    """Oracle scatter == the reference's Triton store_kvcache_kernel, bit for bit."""
+    f = np.load(GOLDEN / "store_kvcache_triton.npz")
+    N, H, KVH, d, nb, bs = (int(x) for x in f["shape"])
+    qkv = f["qkv"]
+    k = np.ascontiguousarray(qkv[:, H * d:(H + KVH) * d]).reshape(N, KVH, d)
+    v = qkv[:, (H + KVH) * d:].reshape(N, KVH, d)  # strided view, as in the engine
+    assert v.strides[0] == qkv.strides[0]
+    kc = np.zeros((nb, bs, KVH, d), np.uint16)
+    vc = np.zeros_like(kc)
+    R.store_kvcache(k, v, kc, vc, f["slot_mapping"])
+    assert np.array_equal(kc, f["k_cache"])
+    assert np.array_equal(vc, f["v_cache"])
+    assert (f["slot_mapping"] == -1).sum() == 2
+
+
+def _states(step):
+    return step["seqs"]
+
+
+def test_prefill_metadata_matches_reference_model_runner():
+    """Restated prepare_prefill == the reference's, on Scheduler/BlockManager states."""
+    fix = json.loads((GOLDEN / "engine_metadata.json").read_text())
+    bs = fix["block_size"]
+    n = 0
+    saw_prefix = saw_chunk = False
+    for step in fix["steps"]:
+        if not step["is_prefill"]:
+            continue
+        cu_q, cu_k, max_q, max_k, slots, tables = R.prepare_prefill_metadata(_states(step), bs)
+        assert cu_q.tolist() == step["cu_seqlens_q"]
+        assert cu_k.tolist() == step["cu_seqlens_k"]
+        assert (max_q, max_k) == (step["max_seqlen_q"], step["max_seqlen_k"])
+        assert slots.tolist() == step["slot_mapping"]
+        assert (tables is None) == (step["block_tables"] is None)
+        if tables is not None:
+            assert tables.tolist() == step["block_tables"]
+            saw_prefix = True
+        saw_chunk |= any(s["start"] + s["num_scheduled"] < s["num_tokens"]
+                         for s in step["seqs"])
+        n += 1
+    assert n >= 3 and saw_prefix and saw_chunk
+
+
+def test_decode_metadata_matches_reference_model_runner():
+    fix = json.loads((GOLDEN / "engine_metadata.json").read_text())
+    bs = fix["block_size"]
+    n = 0
+    for step in fix["steps"]:
+        if step["is_prefill"]:
+            continue
+        slots, lens, tables = R.prepare_decode_metadata(_states(step), bs)
+        assert slots.tolist() == step["slot_mapping"]
+        assert lens.tolist() == step["context_lens"]
+        assert tables.tolist() == step["block_tables"]
+        n += 1
+    assert n >= 5
+
+
+def _oracle_case(c):
+    scale = 128 ** -0.5
+    if c["kind"] == "varlen":
+        bt = None if c["block_table"] is None else c["block_table"].numpy()
+        return R.varlen_attention(c["q"], c["k"], c["v"], c["cu_q"].numpy(), c["cu_k"].numpy(),
+                                  scale, True, bt)
+    return R.decode_attention(c["q"], c["k_cache"], c["v_cache"], c["cache_seqlens"].numpy(),
+                              c["block_table"].numpy(), scale)
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_matches_flash_attn_golden(name):
+    """Oracle == flash-attn (the reference's attention) run on a B200, within bf16 rounding."""
+    path = GOLDEN / "flash_attn_golden.npz"
+    if not path.exists():
+        pytest.skip("flash-attn golden vectors not recorded")
+    g = np.load(path)
+    ref = from_bits(g[name]).float()
+    ours = _oracle_case(make_case(name))
+    assert ref.shape == ours.shape
+    # flash-attn rounds its output to bf16 (and P to bf16 before P@V); the
+    # fp32 oracle does neither: allow a few bf16 ulps of O.
+    err = (ref - ours).abs().max().item()
+    assert err < 1e-2, err
+
+
+def test_chain_tree_equals_paged_causal_prefill():
+    """A chain-shaped tree mask is ordinary bottom-right causal prefill."""
+    c = make_case("chain8")
+    bt = c["block_table"].numpy()
+    cu_q = c["cu_q"].numpy()
+    cu_k = c["cu_k"].numpy()
+    ctx = (np.diff(cu_k) - np.diff(cu_q)).astype(np.int32)
+    masks = np.concatenate([np.array([(1 << (j + 1)) - 1 for j in range(int(n))], np.uint64)
+                            for n in np.diff(cu_q)])
+    a = R.tree_attention(c["q"], c["k"], c["v"], cu_q, ctx, masks, bt, 128 ** -0.5)
+    b = R.varlen_attention(c["q"], c["k"], c["v"], cu_q, cu_k, 128 ** -0.5, True, bt)
+    assert torch.allclose(a, b, atol=1e-6)
+
+
+def test_decode_equals_single_query_prefill():
+    c = make_case("decode")
+    lens = c["cache_seqlens"].numpy()
+    B = len(lens)
+    cu_q = np.arange(B + 1, dtype=np.int32)
+    cu_k = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    a = R.decode_attention(c["q"], c["k_cache"], c["v_cache"], lens, c["block_table"].numpy(),
+                           128 ** -0.5)
+    b = R.varlen_attention(c["q"], c["k_cache"], c["v_cache"], cu_q, cu_k, 128 ** -0.5, True,
+                           c["block_table"].numpy())
+    assert torch.allclose(a, b, atol=1e-6)
+
+
+def test_causal_mask_is_bottom_right_aligned():
+    m = R.causal_allowed(2, 5)
+    assert m.tolist() == [[True, True, True, True, False], [True] * 5]
+    # a row that sees no key produces zeros
+    q = torch.randn(3, 2, 128).bfloat16()
+    k = torch.randn(1, 1, 128).bfloat16()
+    o = R.varlen_attention(q, k, k, [0, 3], [0, 1], 0.1, True)
+    assert torch.all(o[:2] == 0) and torch.any(o[2] != 0)
+
+
+def test_kv_move_reads_before_writes():
+    kc = np.arange(8 * 4, dtype=np.uint16).reshape(1, 8, 1, 4)
+    vc = kc + 1000
+    R.kv_move(kc, vc, np.array([3, 5, 6]), np.array([2, 3, 4]), np.array([0, 3]))
+    assert kc[0, 2, 0, 0] == 12 and kc[0, 3, 0, 0] == 20 and kc[0, 4, 0, 0] == 24
+    assert vc[0, 3, 0, 0] == 1020
