@@ -263,6 +263,7 @@ def run_nvattn(args):
 
     sampler = ClockSampler(local)
     sampler.start()
+    time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
     barrier(world)
     ms = timed(step, args.steps, stream)
     barrier(world)
@@ -534,8 +535,6 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # the CPU reference runs on rank 0 only
-    for _ in range(args.warmup):
-        pass
     vals, last = [], None
     t0 = time.perf_counter()
     for _ in range(max(1, args.steps)):
@@ -562,8 +561,8 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("nvattn", "reference"), default="nvattn")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")

@@ -38,3 +38,24 @@ def cu(lens):
 
 def max_err(a: torch.Tensor, b: torch.Tensor) -> float:
     return (a.float().cpu() - b.float().cpu()).abs().max().item()
+
+
+# Attention-output tolerance: max-abs 1e-2 between the bf16 kernel output and
+# the fp32-accumulated reference, plus the output's own bf16 rounding
+# (half an ulp = 2^-8 of |ref| at worst). Rounding alone reaches 0.0078 for
+# |ref| in [2, 4); flash-attn's outputs on the committed golden cases differ
+# from the fp32 oracle by up to 0.0072 at |ref| = 2.49.
+ATOL = 1e-2
+RTOL = 2.0 ** -8
+
+
+def excess(a: torch.Tensor, b: torch.Tensor) -> float:
+    """max(|a - b| - (ATOL + RTOL |b|)); <= 0 means within tolerance."""
+    a = a.float().cpu()
+    b = b.float().cpu()
+    return ((a - b).abs() - (ATOL + RTOL * b.abs())).max().item()
+
+
+def assert_close(a: torch.Tensor, b: torch.Tensor, what: str = "") -> None:
+    ex = excess(a, b)
+    assert ex <= 0, f"{what}: max-abs error {max_err(a, b):.4g} exceeds 1e-2 + 2^-8|ref| by {ex:.3g}"

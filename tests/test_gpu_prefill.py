@@ -1,19 +1,18 @@
 """Varlen causal prefill (dense and paged/prefix-cache) on the GPU against
-the oracle (max-abs 1e-2)."""
+the oracle (max-abs 1e-2 plus the bf16 output rounding, helpers.ATOL/RTOL)."""
 from __future__ import annotations
 
 import numpy as np
 import pytest
 import torch
 
-from helpers import cu, max_err, paged_layout, random_cache
+from helpers import assert_close, cu, paged_layout, random_cache
 from oracle import reference_math as R
 
 from nvattn import ops
 
 pytestmark = pytest.mark.gpu
 dev = torch.device("cuda")
-TOL = 1e-2
 
 
 def _dense(lens_q, H, KVH, lens_k=None, causal=True, seed=0):
@@ -39,20 +38,20 @@ def _dense(lens_q, H, KVH, lens_k=None, causal=True, seed=0):
 def test_dense_causal(H, KVH):
     lens = [1, 2, 63, 64, 65, 300, 1024]
     out, ref = _dense(lens, H, KVH, seed=H * 3 + KVH)
-    assert max_err(out, ref) < TOL
+    assert_close(out, ref)
     assert ops.read_status() == 0
 
 
 def test_dense_non_causal():
     out, ref = _dense([5, 130, 77], 16, 8, causal=False, seed=2)
-    assert max_err(out, ref) < TOL
+    assert_close(out, ref)
 
 
 def test_dense_fewer_keys_than_queries():
     # bottom-right alignment: the first Lq-Lk queries see no key -> zeros
     out, ref = _dense([6, 10], 8, 4, lens_k=[3, 10], seed=3)
     assert torch.all(out[:3] == 0)
-    assert max_err(out, ref) < TOL
+    assert_close(out, ref)
 
 
 def _paged(cached, new, H, KVH, block_size=256, seed=0, shared_prefix=False):
@@ -82,19 +81,19 @@ def test_paged_prefix_cache_hit_qwen3_8b_shape():
     rng = np.random.default_rng(21)
     new = rng.integers(128, 513, size=4).tolist()
     out, ref = _paged([2048] * 4, new, 32, 8, seed=21, shared_prefix=True)
-    assert max_err(out, ref) < TOL
+    assert_close(out, ref)
     assert ops.read_status() == 0
 
 
 def test_paged_chunked_prefill_continuation():
     # second chunk of a chunked prefill: 1024 cached tokens, 276 new (scheduler.py:42)
     out, ref = _paged([1024, 0, 300], [276, 50, 1], 16, 8, seed=22)
-    assert max_err(out, ref) < TOL
+    assert_close(out, ref)
 
 
 def test_paged_unaligned_prefix_and_block_512():
     out, ref = _paged([100, 700], [33, 64], 16, 4, block_size=512, seed=23)
-    assert max_err(out, ref) < TOL
+    assert_close(out, ref)
 
 
 def test_flash_attn_varlen_func_keyword_form():
@@ -109,4 +108,4 @@ def test_flash_attn_varlen_func_keyword_form():
                                    cu_seqlens_k=c.to(dev), softmax_scale=128 ** -0.5,
                                    causal=True, block_table=None)
     ref = R.varlen_attention(q, k, v, c.numpy(), c.numpy(), 128 ** -0.5, True)
-    assert max_err(o, ref) < TOL
+    assert_close(o, ref)

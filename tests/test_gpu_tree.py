@@ -6,14 +6,13 @@ import pytest
 import torch
 
 from conftest import bf16_bits
-from helpers import cu, max_err, paged_layout, random_cache
+from helpers import assert_close, cu, max_err, paged_layout, random_cache
 from oracle import reference_math as R
 
 from nvattn import ops, tree
 
 pytestmark = pytest.mark.gpu
 dev = torch.device("cuda")
-TOL = 1e-2
 
 
 def _setup(ctx, n_nodes, H, KVH, seed):
@@ -55,7 +54,7 @@ def test_eagle_tree_64_nodes_qwen3_8b_shape():
                     kc.view(torch.int16).numpy(), vc.view(torch.int16).numpy(), slots.numpy())
     assert torch.equal(kcd.cpu(), kc) and torch.equal(vcd.cpu(), vc)
     ref = R.tree_attention(q, kc, vc, cq.numpy(), ctx, all_masks, bt.numpy(), 128 ** -0.5)
-    assert max_err(out, ref) < TOL
+    assert_close(out, ref)
     assert ops.read_status() == 0
 
 
@@ -75,8 +74,10 @@ def test_chain_draft_equals_paged_prefill_kernel():
                            causal=True, block_table=bt.to(dev))
     torch.cuda.synchronize()
     ref = R.varlen_attention(q, kc, vc, cq.numpy(), ck.numpy(), 128 ** -0.5, True, bt.numpy())
-    assert max_err(a, ref) < TOL and max_err(b, ref) < TOL
-    assert max_err(a, b) < 4e-3
+    assert_close(a, ref)
+    assert_close(b, ref)
+    # same kernel family, same masks: the two paths agree to bf16 rounding
+    assert max_err(a, b) <= 2 ** -7 * max(1.0, float(ref.abs().max()))
 
 
 def test_accepted_path_compaction():

@@ -92,9 +92,9 @@ def test_oracle_matches_flash_attn_golden(name):
     ours = _oracle_case(make_case(name))
     assert ref.shape == ours.shape
     # flash-attn rounds its output to bf16 (and P to bf16 before P@V); the
-    # fp32 oracle does neither: allow a few bf16 ulps of O.
-    err = (ref - ours).abs().max().item()
-    assert err < 1e-2, err
+    # fp32 oracle does neither: max-abs 1e-2 plus the output's bf16 rounding.
+    from helpers import excess
+    assert excess(ref, ours) <= 0, (ref - ours).abs().max().item()
 
 
 def test_chain_tree_equals_paged_causal_prefill():
