@@ -166,6 +166,38 @@ NVATTN_API int nvattn_paged_decode(const void* q, int64_t q_stride_tok, int64_t 
                         int32_t* status, void* stream);
 
 /*
+ * Allocation-free paged decode (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory when they run decode: a host
+ * whose allocator already gave the free device memory to the KV cache, a path
+ * that must not take cudaMalloc's implicit device-wide synchronisation, or a
+ * foreign-language host that holds only pointers. Arguments and results are
+ * those of nvattn_paged_decode without the workspace: the split-K partials go
+ * to a fixed array of device memory inside the library, 16 MiB
+ * (16777216 bytes) on every GPU that loads the library, held until the
+ * process exits. A batch whose
+ * workspace (nvattn_decode_workspace_bytes) exceeds it is rejected with
+ * NVATTN_ERR_WORKSPACE before any launch. Nothing is allocated, by the library
+ * or by anything it calls.
+ *
+ * The first call on a device looks up the array's device address (with that
+ * device current) and caches it; make that first call before any stream
+ * capture on the device. All calls on a device share the one array and it
+ * keeps the last call's contents (nothing in it has to start at zero): calls
+ * whose executions can overlap on the GPU (different streams without
+ * ordering between them) race on it and must be serialised by the caller.
+ */
+NVATTN_API int nvattn_paged_decode_noalloc(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                const void* k_cache, const void* v_cache,
+                                void* out, int64_t o_stride_tok, int64_t o_stride_head,
+                                const int32_t* cache_seqlens,
+                                const int32_t* block_table, int64_t block_table_stride,
+                                int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
+                                int32_t batch, int32_t num_heads, int32_t num_kv_heads,
+                                int32_t head_dim, float softmax_scale,
+                                int32_t* status, void* stream);
+
+/*
  * Tree-verification attention (no counterpart in the reference: EAGLE3-style
  * speculative verification, new in this library).
  *

@@ -520,3 +520,81 @@ extern "C" int nvattn_paged_decode(const void* q, int64_t q_stride_tok, int64_t 
   }
   return NVATTN_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode.
+//
+// nvattn_paged_decode needs a split-K workspace from its caller. Some callers
+// cannot allocate device memory at the point where they run decode: a host
+// whose memory manager has already handed the rest of the GPU to the KV cache
+// (Nano-vLLM-X sizes its cache to fill gpu_memory_utilization of the device,
+// model_runner.py:103-121), a path that must not take cudaMalloc's implicit
+// device-wide synchronisation, or a foreign-language host that only holds
+// pointers and has no CUDA allocator. For them this variant keeps the
+// workspace in a fixed array of device memory that belongs to the library:
+// each GPU that loads libnvattn.so holds kNoAllocScratchBytes of it until the
+// process exits.
+namespace nvattn {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// symbol itself is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+static int noalloc_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[kNoAllocMaxDevices] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "paged_decode_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode_noalloc: device index >= 64");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "paged_decode_noalloc: cudaGetSymbolAddress");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return NVATTN_OK;
+}
+
+}  // namespace nvattn
+
+extern "C" int nvattn_paged_decode_noalloc(
+    const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* k_cache,
+    const void* v_cache, void* out, int64_t o_stride_tok, int64_t o_stride_head,
+    const int32_t* cache_seqlens, const int32_t* block_table, int64_t block_table_stride,
+    int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size, int32_t batch,
+    int32_t num_heads, int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+    int32_t* status, void* stream) {
+  using namespace nvattn;
+  clear_error();
+  const size_t need = nvattn_decode_workspace_bytes(batch, num_heads, num_kv_heads,
+                                                    max_blocks_per_seq, block_size);
+  if (need > kNoAllocScratchBytes) {
+    char buf[200];
+    snprintf(buf, sizeof(buf),
+             "paged_decode_noalloc: this batch needs %zu bytes of split-K workspace, more than "
+             "the library's fixed %zu-byte scratch; use nvattn_paged_decode with a workspace",
+             need, kNoAllocScratchBytes);
+    return fail(NVATTN_ERR_WORKSPACE, buf);
+  }
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int rc = noalloc_scratch_address(&scratch);
+    if (rc) return rc;
+  }
+  // Same kernels as nvattn_paged_decode; only the workspace differs. Every
+  // partial a call reads is written earlier in that same call, so the
+  // scratch needs no clearing between calls.
+  return nvattn_paged_decode(q, q_stride_tok, q_stride_head, k_cache, v_cache, out, o_stride_tok,
+                             o_stride_head, cache_seqlens, block_table, block_table_stride,
+                             max_blocks_per_seq, num_blocks, block_size, batch, num_heads,
+                             num_kv_heads, head_dim, softmax_scale, scratch,
+                             need > 0 ? kNoAllocScratchBytes : 0, status, stream);
+}

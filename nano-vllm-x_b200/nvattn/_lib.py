@@ -51,6 +51,10 @@ SIGNATURES: dict[str, tuple] = {
                                     c_int32, c_int32, c_int32,
                                     c_int32, c_int32, c_int32, c_int32,
                                     c_float, _P, c_size_t, _I32P, _P]),
+    "nvattn_paged_decode_noalloc": (c_int, [_P, c_int64, c_int64, _P, _P, _P, c_int64, c_int64,
+                                            _I32P, _I32P, c_int64, c_int32, c_int32, c_int32,
+                                            c_int32, c_int32, c_int32, c_int32, c_float, _I32P,
+                                            _P]),
     "nvattn_tree_verify": (c_int, [_P, c_int64, c_int64,
                                    _P, _P,
                                    _P, c_int64, c_int64,
