@@ -57,16 +57,16 @@ WORKLOAD = ("configs[3] long-context paged decode, Qwen3-32B attention: 64Q/8KV 
 
 # ----------------------------------------------------------------- workload
 
-def decode_workload(seed: int = 0):
+def decode_workload(seed: int = 0, batch: int = BATCH):
     rng = np.random.default_rng(seed)
-    lens = rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int32)
+    lens = rng.integers(CTX_LO, CTX_HI + 1, size=batch).astype(np.int32)
     nblk = (lens + BS - 1) // BS
     total = int(nblk.sum())
     perm = rng.permutation(total).astype(np.int32)
     width = int(nblk.max())
-    bt = np.full((BATCH, width), -1, np.int32)
+    bt = np.full((batch, width), -1, np.int32)
     pos = 0
-    for b in range(BATCH):
+    for b in range(batch):
         bt[b, :nblk[b]] = perm[pos:pos + nblk[b]]
         pos += nblk[b]
     return lens, bt, total
@@ -221,7 +221,8 @@ def run_nvattn(args):
     H, KVH = q1 - q0, k1 - k0
     hbm_peak, tf_peak, tf_sus, peak_src = load_peaks()
 
-    lens, bt_np, nblocks = decode_workload(0)
+    BATCH = args.batch  # noqa: N806  (configs[3] uses 128; smaller only for profiling)
+    lens, bt_np, nblocks = decode_workload(0, BATCH)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     kv = torch.empty(2, nblocks, BS, KVH, D, dtype=torch.bfloat16, device=dev)
     kv.normal_(generator=g)
@@ -344,7 +345,8 @@ def run_nvattn(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 K/V/Q; numpy seed 0 lengths and block permutation)",
-            "config": {"workload": WORKLOAD, "global_batch": BATCH, "num_heads": H_TOTAL,
+            "config": {"workload": WORKLOAD if BATCH == 128 else WORKLOAD + f" (batch {BATCH})",
+                       "global_batch": BATCH, "num_heads": H_TOTAL,
                        "num_kv_heads": KVH_TOTAL, "head_dim": D, "block_size": BS,
                        "ctx_range": [CTX_LO, CTX_HI], "parallelism": f"tp{world} (head-sharded)",
                        "l2": "inputs larger than L2 (KV cache >= 1.2 GB per rank vs 126 MB L2)"},
@@ -564,6 +566,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("nvattn", "reference"), default="nvattn")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="decode batch (configs[3] = 128; smaller values only for ncu captures)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
