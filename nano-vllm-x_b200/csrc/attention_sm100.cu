@@ -1,0 +1,659 @@
+// Varlen causal prefill (dense and paged / prefix-cache) and tree-verification
+// attention on the 5th-generation tensor cores. Replaces flash_attn_varlen_func
+// as called at nanovllm/layers/attention.py:64-70; the tree mode (EAGLE-style
+// speculative verification) has no counterpart in the reference.
+//
+// CTA = (row block m, KV head g, sequence b). Rows are GQA-packed: row
+// (token t, head-in-group hh) of the sequence is t*group + hh, so one K/V tile
+// serves every query head of the group. A CTA owns two 128-row Q tiles.
+//
+// Warp roles (10 warps):
+//   warp 0      TMA producer: both Q tiles once, then 128-key K and V tiles
+//               through a 2-stage mbarrier ring (3-D map over the dense K/V
+//               projections or 4-D map over the paged cache; 128-byte
+//               swizzle; no multicast).
+//   warp 1      owns the TMEM allocation (512 columns) and issues every
+//               tcgen05.mma from one thread:
+//                 S_i = Q_i K^T   (M=128, N=128 keys, K=128 dims; A and B from
+//                                  shared memory, K-major)
+//                 O_i += P_i V    (M=128, N=128 dims, K=128 keys; A = P from
+//                                  TMEM, B = V from shared memory, MN-major)
+//               ordered S0, S1, then per key tile: PV0_j, S0_{j+1}, PV1_j,
+//               S1_{j+1}, so one warpgroup's softmax overlaps the other's MMAs.
+//   warps 2-5   softmax warpgroup for Q tile 0, warps 6-9 for Q tile 1. A
+//               thread owns one row: it reads its 128 scores from TMEM, masks
+//               and scales them, keeps the row max and sum in registers, and
+//               writes P (bf16 pairs) back over S in TMEM. The output is
+//               rescaled only when the running max grows by more than 2^8
+//               (P then stays <= 256; the final O/l is unchanged), so the
+//               O read-modify-write in TMEM is rare.
+// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512).
+//
+// Masks (query token i of the sequence, key j):
+//   causal (dense/paged): j <= seqlen_k - seqlen_q + i   (bottom-right aligned)
+//   tree: j < context_len, or bit (j - context_len) of the row's mask word.
+// Keys past the sequence's end in the last tile of the paged cache are stale
+// bytes (maybe NaN): their scores are masked and their V rows zeroed in
+// shared memory before the P V product.
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "sm100.cuh"
+
+namespace nvattn {
+namespace tc {
+
+constexpr int kBM = 128;                 // rows per Q tile
+constexpr int kBN = 128;                 // keys per K/V tile
+constexpr int kHalf = 128 * 128;         // 128 rows x 128 B (64 bf16) = 16 KB
+constexpr int kOperand = 2 * kHalf;      // one 128 x 128 bf16 operand = 32 KB
+constexpr int kStages = 2;
+constexpr int kQBytes = 2 * kOperand;                       // Q0, Q1
+constexpr int kRingBytes = kStages * 2 * kOperand;          // K and V per stage
+constexpr int kSmemData = kQBytes + kRingBytes;             // 192 KB
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+// TMEM column of S_i (later P_i) and O_i
+__device__ __forceinline__ uint32_t col_s(int i) { return static_cast<uint32_t>(i) * 128u; }
+__device__ __forceinline__ uint32_t col_o(int i) { return 256u + static_cast<uint32_t>(i) * 128u; }
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
+
+enum Mode { kDense = 0, kPaged = 1, kTree = 2 };
+
+struct Params {
+  __nv_bfloat16* out;
+  int64_t o_stride_tok, o_stride_head;
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  const int32_t* ctx_lens;
+  const uint64_t* tree_mask;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int64_t total_q;
+  int32_t max_blocks, num_blocks, block_size, num_kv_heads, group;
+  int32_t tpt;  // query tokens per Q tile (floor(128 / group))
+  int32_t rpt;  // rows per Q tile (group * tpt <= 128)
+  int32_t causal;
+  int32_t out_vec16;  // output rows 16-byte aligned
+  float scale_log2;
+  int32_t* status;
+};
+
+struct Barriers {
+  uint64_t q_full;
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ uint64_t kdesc(uint32_t base, int kk) {
+  // K-major operand (Q or K): 16-dim step kk lives in half kk/4 at +32*(kk%4) B.
+  return sm100::sw128_desc(base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+}
+
+__device__ __forceinline__ uint64_t vdesc(uint32_t base, int kk) {
+  // MN-major V: 16-key step kk starts at row 16*kk; the two 64-dim halves are
+  // kHalf apart (leading byte offset), 8-row groups 1024 B apart (stride).
+  return sm100::sw128_desc(base + kk * 16 * 128, kHalf, 1024);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                   const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const Params p) {
+  const int b = blockIdx.z;
+  const int g = blockIdx.y;
+  const int m = gridDim.x - 1 - blockIdx.x;  // heaviest row blocks first
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ------------------------------------------------ sequence geometry
+  const int q_begin = p.cu_q[b];
+  int Lq = p.cu_q[b + 1] - q_begin;
+  if (q_begin < 0 || q_begin > p.total_q) return;
+  if (q_begin + static_cast<int64_t>(Lq) > p.total_q) Lq = static_cast<int>(p.total_q - q_begin);
+  int Lk, k_begin = 0, ctx = 0;
+  if (MODE == kTree) {
+    ctx = p.ctx_lens[b];
+    Lk = ctx + Lq;
+  } else {
+    k_begin = p.cu_k[b];
+    Lk = p.cu_k[b + 1] - k_begin;
+  }
+  if (MODE != kDense && Lk > p.max_blocks * p.block_size) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) set_status(p.status, NVATTN_STATUS_BAD_BLOCK);
+    const int cut = Lk - p.max_blocks * p.block_size;
+    Lk -= cut;
+    if (MODE == kTree) ctx = max(0, ctx - cut);
+  }
+  const int group = p.group;
+  const int tok0 = m * 2 * p.tpt;  // first query token of this CTA
+  if (Lq <= 0 || tok0 >= Lq) return;
+  const int tok_hi = min(Lq - 1, tok0 + 2 * p.tpt - 1);
+  const int diag = Lk - Lq;
+  int kend;
+  if (MODE == kTree)
+    kend = Lk;
+  else
+    kend = p.causal ? min(Lk, diag + tok_hi + 1) : Lk;
+  const int ntiles = kend > 0 ? (kend + kBN - 1) / kBN : 0;
+
+  if (ntiles == 0) {
+    // No visible key for any row of this CTA: the rows are zeros.
+    for (int e = threadIdx.x; e < 2 * p.rpt * (kHeadDim / 8); e += blockDim.x) {
+      const int r = e / (kHeadDim / 8), c = e % (kHeadDim / 8);
+      const int tok = tok0 + (r / p.rpt) * p.tpt + (r % p.rpt) / group;
+      if (tok >= Lq || tok > tok0 + 2 * p.tpt - 1) continue;
+      __nv_bfloat16* o = p.out + static_cast<int64_t>(q_begin + tok) * p.o_stride_tok +
+                         static_cast<int64_t>(g * group + (r % p.rpt) % group) * p.o_stride_head;
+      for (int d = 0; d < 8; ++d) o[c * 8 + d] = __float2bfloat16_rn(0.f);
+    }
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kSmemData);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t q_s[2] = {sbase, sbase + kOperand};
+  auto k_s = [&](int st) { return sbase + kQBytes + st * 2 * kOperand; };
+  auto v_s = [&](int st) { return sbase + kQBytes + st * 2 * kOperand + kOperand; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bars->kv_full[s], 1);
+      mbar_init(&bars->kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      mbar_init(&bars->p_full[i], 4);
+    }
+    mbar_init(&bars->o_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(&bars->tmem_base, kTmemCols);
+    sm100::tmem_relinquish();
+  }
+  sm100::fence_before_sync();
+  __syncthreads();
+  sm100::fence_after_sync();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tensor_map(&qmap);
+      prefetch_tensor_map(&kmap);
+      prefetch_tensor_map(&vmap);
+      const uint32_t qbytes = 2u * 2u * static_cast<uint32_t>(p.rpt) * 128u;
+      mbar_arrive_expect_tx(&bars->q_full, qbytes);
+      for (int i = 0; i < 2; ++i) {
+        const int row = q_begin + tok0 + i * p.tpt;
+        tma_load_3d(smem + i * kOperand, &qmap, &bars->q_full, 0, g * group, row);
+        tma_load_3d(smem + i * kOperand + kHalf, &qmap, &bars->q_full, 64, g * group, row);
+      }
+      const int32_t* bt =
+          (MODE == kDense) ? nullptr : p.block_table + static_cast<int64_t>(b) * p.bt_stride;
+      int issued = 0;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % kStages;
+        if (!mbar_wait(&bars->kv_empty[st], ((j / kStages) & 1) ^ 1)) {
+          set_status(p.status, NVATTN_STATUS_TIMEOUT);
+          break;
+        }
+        const int j0 = j * kBN;
+        uint8_t* kd = smem + kQBytes + st * 2 * kOperand;
+        uint8_t* vd = kd + kOperand;
+        mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kOperand);
+        if (MODE == kDense) {
+          const int row = k_begin + j0;
+          tma_load_3d(kd, &kmap, &bars->kv_full[st], 0, g, row);
+          tma_load_3d(kd + kHalf, &kmap, &bars->kv_full[st], 64, g, row);
+          tma_load_3d(vd, &vmap, &bars->kv_full[st], 0, g, row);
+          tma_load_3d(vd + kHalf, &vmap, &bars->kv_full[st], 64, g, row);
+        } else {
+          int blk = bt[j0 / p.block_size];
+          if (blk < 0 || blk >= p.num_blocks) {
+            set_status(p.status, NVATTN_STATUS_BAD_BLOCK);
+            blk = 0;
+          }
+          const int tin = j0 % p.block_size;
+          tma_load_4d(kd, &kmap, &bars->kv_full[st], 0, g, tin, blk);
+          tma_load_4d(kd + kHalf, &kmap, &bars->kv_full[st], 64, g, tin, blk);
+          tma_load_4d(vd, &vmap, &bars->kv_full[st], 0, g, tin, blk);
+          tma_load_4d(vd + kHalf, &vmap, &bars->kv_full[st], 64, g, tin, blk);
+        }
+        issued = j + 1;
+      }
+      // Drain: no copy of ours may still be in flight when the CTA ends. The
+      // last use of each ring slot is the last phase that barrier completes.
+      mbar_wait(&bars->q_full, 0);
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        mbar_wait(&bars->kv_full[j % kStages], (j / kStages) & 1);
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = sm100::idesc_bf16_f32(kBM, kBN, false);
+      constexpr uint32_t idesc_o = sm100::idesc_bf16_f32(kBM, kHeadDim, true);
+      bool ok = mbar_wait(&bars->q_full, 0);
+      auto issue_s = [&](int i, int st) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          sm100::mma_ss(tmem + col_s(i), kdesc(q_s[i], kk), kdesc(k_s(st), kk), idesc_s,
+                        kk > 0 ? 1u : 0u);
+        sm100::commit(&bars->s_full[i]);
+      };
+      auto issue_pv = [&](int i, int st, int j) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          sm100::mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, vdesc(v_s(st), kk), idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      if (ok) ok = mbar_wait(&bars->kv_full[0], 0);
+      if (ok) {
+        sm100::fence_after_sync();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        const int st = j % kStages;
+        const int nst = (j + 1) % kStages;
+        const bool more = j + 1 < ntiles;
+        ok = mbar_wait(&bars->p_full[0], j & 1);
+        if (!ok) break;
+        sm100::fence_after_sync();
+        issue_pv(0, st, j);
+        if (more) {
+          ok = mbar_wait(&bars->kv_full[nst], ((j + 1) / kStages) & 1);
+          if (!ok) break;
+          sm100::fence_after_sync();
+          issue_s(0, nst);
+        }
+        ok = mbar_wait(&bars->p_full[1], j & 1);
+        if (!ok) break;
+        sm100::fence_after_sync();
+        issue_pv(1, st, j);
+        sm100::commit(&bars->kv_empty[st]);
+        if (more) issue_s(1, nst);
+      }
+      if (!ok) set_status(p.status, NVATTN_STATUS_TIMEOUT);
+      // All MMAs done -> O final; also makes sure none is in flight at exit.
+      sm100::commit(&bars->o_done);
+      mbar_wait(&bars->o_done, 0);
+    }
+  } else {
+    // ----------------------------------------------------------- softmax
+    const int wg = (warp - 2) >> 2;            // Q tile 0 or 1
+    const int quarter = warp & 3;              // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;         // row inside the Q tile
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int tok = tok0 + wg * p.tpt + r / group;
+    const int hh = r % group;
+    const bool valid = r < p.rpt && tok < Lq;
+    const int lim = valid ? ((MODE != kTree && p.causal) ? min(Lk - 1, diag + tok) : Lk - 1) : -1;
+    uint64_t mword = 0;
+    if (MODE == kTree && valid) mword = p.tree_mask[q_begin + tok];
+    // first key index at which this row needs masking
+    const int mask_from = !valid ? 0 : (MODE == kTree ? ctx : lim + 1);
+
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      // warp-uniform: the TMEM loads below are warp-collective
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[wg], j & 1))) {
+        ok = false;
+        break;
+      }
+      sm100::fence_after_sync();
+      const int j0 = j * kBN;
+      const bool full_row = j0 + kBN <= mask_from;  // no key of this tile is masked
+      // Scaled (and masked) score of column e of a 32-column chunk.
+      auto score = [&](uint32_t raw, int key) -> float {
+        const float x = __uint_as_float(raw) * p.scale_log2;
+        if (full_row) return x;
+        bool okk;
+        if (MODE == kTree) {
+          const int t = key - ctx;
+          okk = valid && (t < 0 || (t < Lq && ((mword >> t) & 1ull)));
+        } else {
+          okk = key <= lim;
+        }
+        return okk ? x : -INFINITY;
+      };
+      // Pass 1: row max over the tile (32 columns in registers at a time).
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        sm100::tmem_ld32(t_lane + col_s(wg) + c * 32, sr);
+        sm100::tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, score(sr[e], j0 + c * 32 + e));
+      }
+      // Lazy rescale: keep the reference max unless the row max grew by > 2^8.
+      float alpha = 1.f;
+      bool need = false;
+      if (mx > m_used + kRescaleThreshold) {
+        need = (m_used != -INFINITY);  // nothing accumulated yet otherwise
+        alpha = need ? fast_exp2(m_used - mx) : 1.f;
+        m_used = mx;
+        l *= alpha;
+      }
+      const float base = (m_used == -INFINITY) ? 0.f : m_used;
+      // Pass 2: P = exp2(score - base) as bf16 pairs, written over S. Chunk c
+      // of S (columns 32c..32c+31) becomes P columns 16c..16c+15; chunk c is
+      // read before any store can reach its columns.
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        sm100::tmem_ld32(t_lane + col_s(wg) + c * 32, sr);
+        sm100::tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = fast_exp2(score(sr[2 * e], j0 + c * 32 + 2 * e) - base);
+          const float p1 = fast_exp2(score(sr[2 * e + 1], j0 + c * 32 + 2 * e + 1) - base);
+          sum += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        sm100::tmem_st16(t_lane + col_s(wg) + c * 16, pk);
+      }
+      l += sum;
+      // O rescale after P is out of registers (keeps the score row and this
+      // buffer from being live together).
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        uint32_t orr[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          sm100::tmem_ld32(t_lane + col_o(wg) + c * 32, orr);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+          sm100::tmem_st32(t_lane + col_o(wg) + c * 32, orr);
+        }
+      }
+      if (MODE != kDense && wg == 0 && j == ntiles - 1 && kend - j0 < kBN) {
+        // Stale cache rows past the end of the sequence: zero their V so that
+        // 0 * NaN cannot reach O. Every tile row r is one 128-byte line in
+        // each half.
+        const int vlim = kend - j0;
+        if (r >= vlim) {
+          uint8_t* vrow = smem + kQBytes + (j % kStages) * 2 * kOperand + kOperand + r * 128;
+          const int4 z = make_int4(0, 0, 0, 0);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            reinterpret_cast<int4*>(vrow)[c] = z;
+            reinterpret_cast<int4*>(vrow + kHalf)[c] = z;
+          }
+        }
+        fence_proxy_async();
+      }
+      sm100::tmem_wait_st();
+      sm100::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->p_full[wg]);
+    }
+    if (!ok && lane == 0) set_status(p.status, NVATTN_STATUS_TIMEOUT);
+
+    // ----------------------------------------------------------- epilogue
+    const bool done = __all_sync(0xffffffffu, mbar_wait(&bars->o_done, 0));
+    sm100::fence_after_sync();
+    const float inv = (l > 0.f) ? 1.f / l : 0.f;
+    __nv_bfloat16* orow = p.out + static_cast<int64_t>(q_begin + (valid ? tok : 0)) * p.o_stride_tok +
+                          static_cast<int64_t>(g * group + hh) * p.o_stride_head;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t orr[32];
+      sm100::tmem_ld32(t_lane + col_o(wg) + c * 32, orr);
+      sm100::tmem_wait_ld();
+      if (valid && done) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack_bf16x2(__uint_as_float(orr[2 * e]) * inv,
+                              __uint_as_float(orr[2 * e + 1]) * inv);
+        if (p.out_vec16) {
+          int4* dst = reinterpret_cast<int4*>(orow + c * 32);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[e] = make_int4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+        } else {
+          uint32_t* dst = reinterpret_cast<uint32_t*>(orow + c * 32);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) dst[e] = pk[e];
+        }
+      }
+    }
+    if (!done && lane == 0) set_status(p.status, NVATTN_STATUS_TIMEOUT);
+  }
+
+  // Every TMEM access of this CTA is complete: release the allocation.
+  sm100::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    sm100::fence_after_sync();
+    sm100::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int make_kv_map(CUtensorMap* map, const void* base, bool paged, int64_t total, int num_blocks,
+                int block_size, int num_kv_heads, int64_t stride_tok, int64_t stride_head) {
+  if (paged) {
+    const uint64_t dims[4] = {static_cast<uint64_t>(kHeadDim),
+                              static_cast<uint64_t>(num_kv_heads),
+                              static_cast<uint64_t>(block_size),
+                              static_cast<uint64_t>(num_blocks)};
+    const uint64_t strides[3] = {
+        static_cast<uint64_t>(kHeadDim) * 2, static_cast<uint64_t>(num_kv_heads) * kHeadDim * 2,
+        static_cast<uint64_t>(block_size) * num_kv_heads * kHeadDim * 2};
+    const uint32_t box[4] = {64, 1, static_cast<uint32_t>(kBN), 1};
+    return make_tensor_map(map, base, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(num_kv_heads),
+                            static_cast<uint64_t>(total)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(stride_head) * 2,
+                               static_cast<uint64_t>(stride_tok) * 2};
+  const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kBN)};
+  return make_tensor_map(map, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int make_q_map(CUtensorMap* map, const void* q, int64_t total_q, int num_heads, int64_t stride_tok,
+               int64_t stride_head, int group, int tpt) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(num_heads),
+                            static_cast<uint64_t>(total_q)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(stride_head) * 2,
+                               static_cast<uint64_t>(stride_tok) * 2};
+  const uint32_t box[3] = {64, static_cast<uint32_t>(group), static_cast<uint32_t>(tpt)};
+  return make_tensor_map(map, q, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+constexpr int kSmemBytes = kSmemData + 1024 + static_cast<int>(sizeof(Barriers)) + 64;
+
+template <int MODE>
+int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
+           int num_seqs, int max_tokens, cudaStream_t stream) {
+  static std::mutex mu;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 64 || !attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<MODE>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kSmemBytes);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tc_kernel)");
+      if (dev < 64) attr_done[dev] = true;
+    }
+  }
+  const int blocks_m = (max_tokens + 2 * p.tpt - 1) / (2 * p.tpt);
+  if (blocks_m <= 0) return NVATTN_OK;
+  if (num_seqs > 65535) return fail(NVATTN_ERR_UNSUPPORTED, "more than 65535 sequences");
+  dim3 grid(blocks_m, p.num_kv_heads, num_seqs);
+  attn_tc_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "attn_tc_kernel launch");
+  return NVATTN_OK;
+}
+
+}  // namespace tc
+
+// Shared argument checks of the two entry points; returns NVATTN_OK or a code.
+static int tc_check_q_out(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                          const void* out, int64_t o_stride_tok, int64_t o_stride_head,
+                          int num_heads, int num_kv_heads, int head_dim, const char* who) {
+  if (!q || !out) return fail(NVATTN_ERR_INVALID, std::string(who) + ": NULL q/out");
+  if (head_dim != kHeadDim)
+    return fail(NVATTN_ERR_UNSUPPORTED, std::string(who) + ": head_dim must be 128");
+  if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads)
+    return fail(NVATTN_ERR_INVALID,
+                std::string(who) + ": num_heads must be a multiple of num_kv_heads");
+  if (num_heads / num_kv_heads > 16)
+    return fail(NVATTN_ERR_UNSUPPORTED,
+                std::string(who) + ": more than 16 query heads per KV head");
+  if (!aligned16(q) || (q_stride_tok * 2) % 16 || (q_stride_head * 2) % 16)
+    return fail(NVATTN_ERR_UNSUPPORTED,
+                std::string(who) + ": q base and strides must be 16-byte multiples (TMA)");
+  if ((reinterpret_cast<uintptr_t>(out) & 3) || (o_stride_tok & 1) || (o_stride_head & 1))
+    return fail(NVATTN_ERR_UNSUPPORTED, std::string(who) + ": out rows must be 4-byte aligned");
+  return NVATTN_OK;
+}
+
+static tc::Params tc_params(void* out, int64_t o_stride_tok, int64_t o_stride_head,
+                            int num_heads, int num_kv_heads, float softmax_scale,
+                            int64_t total_q, int32_t* status) {
+  tc::Params p{};
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_stride_tok = o_stride_tok;
+  p.o_stride_head = o_stride_head;
+  p.total_q = total_q;
+  p.num_kv_heads = num_kv_heads;
+  p.group = num_heads / num_kv_heads;
+  p.tpt = tc::kBM / p.group;
+  p.rpt = p.tpt * p.group;
+  p.out_vec16 = aligned16(out) && (o_stride_tok * 2) % 16 == 0 && (o_stride_head * 2) % 16 == 0;
+  p.scale_log2 = softmax_scale * kLog2e;
+  p.status = status;
+  return p;
+}
+
+}  // namespace nvattn
+
+using namespace nvattn;
+
+extern "C" int nvattn_varlen_prefill(
+    const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* k,
+    int64_t k_stride_tok, int64_t k_stride_head, const void* v, int64_t v_stride_tok,
+    int64_t v_stride_head, void* out, int64_t o_stride_tok, int64_t o_stride_head,
+    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int32_t num_seqs,
+    int32_t max_seqlen_q, int32_t max_seqlen_k, int64_t total_q, int64_t total_k,
+    const int32_t* block_table, int64_t block_table_stride, int32_t max_blocks_per_seq,
+    int32_t num_blocks, int32_t block_size, int32_t num_heads, int32_t num_kv_heads,
+    int32_t head_dim, float softmax_scale, int32_t causal, int32_t* status, void* stream) {
+  clear_error();
+  if (num_seqs < 0 || total_q < 0 || total_k < 0 || max_seqlen_q < 0 || max_seqlen_k < 0)
+    return fail(NVATTN_ERR_INVALID, "varlen_prefill: negative size");
+  if (num_seqs == 0 || total_q == 0 || max_seqlen_q == 0) return NVATTN_OK;
+  int rc = tc_check_q_out(q, q_stride_tok, q_stride_head, out, o_stride_tok, o_stride_head,
+                          num_heads, num_kv_heads, head_dim, "varlen_prefill");
+  if (rc) return rc;
+  if (!k || !v || !cu_seqlens_q || !cu_seqlens_k)
+    return fail(NVATTN_ERR_INVALID, "varlen_prefill: NULL k/v/cu_seqlens");
+  tc::Params p = tc_params(out, o_stride_tok, o_stride_head, num_heads, num_kv_heads,
+                           softmax_scale, total_q, status);
+  CUtensorMap qm, km, vm;
+  rc = tc::make_q_map(&qm, q, total_q, num_heads, q_stride_tok, q_stride_head, p.group, p.tpt);
+  if (rc) return rc;
+  if (block_table) {
+    if (block_size <= 0 || block_size % tc::kBN)
+      return fail(NVATTN_ERR_UNSUPPORTED, "varlen_prefill: block_size must be a multiple of 128");
+    if (num_blocks <= 0 || max_blocks_per_seq <= 0 || block_table_stride < max_blocks_per_seq)
+      return fail(NVATTN_ERR_INVALID, "varlen_prefill: bad block table geometry");
+    if (!aligned16(k) || !aligned16(v))
+      return fail(NVATTN_ERR_INVALID, "varlen_prefill: caches must be 16-byte aligned");
+    rc = tc::make_kv_map(&km, k, true, 0, num_blocks, block_size, num_kv_heads, 0, 0);
+    if (rc) return rc;
+    rc = tc::make_kv_map(&vm, v, true, 0, num_blocks, block_size, num_kv_heads, 0, 0);
+    if (rc) return rc;
+  } else {
+    if (total_k <= 0) return fail(NVATTN_ERR_INVALID, "varlen_prefill: total_k must be > 0");
+    if (!aligned16(k) || !aligned16(v) || (k_stride_tok * 2) % 16 || (k_stride_head * 2) % 16 ||
+        (v_stride_tok * 2) % 16 || (v_stride_head * 2) % 16)
+      return fail(NVATTN_ERR_UNSUPPORTED,
+                  "varlen_prefill: k/v base and strides must be 16-byte multiples (TMA)");
+    rc = tc::make_kv_map(&km, k, false, total_k, 0, 0, num_kv_heads, k_stride_tok, k_stride_head);
+    if (rc) return rc;
+    rc = tc::make_kv_map(&vm, v, false, total_k, 0, 0, num_kv_heads, v_stride_tok, v_stride_head);
+    if (rc) return rc;
+  }
+  p.cu_q = cu_seqlens_q;
+  p.cu_k = cu_seqlens_k;
+  p.block_table = block_table;
+  p.bt_stride = block_table_stride;
+  p.max_blocks = block_table ? max_blocks_per_seq : 0;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.causal = causal ? 1 : 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return block_table ? tc::launch<tc::kPaged>(qm, km, vm, p, num_seqs, max_seqlen_q, s)
+                     : tc::launch<tc::kDense>(qm, km, vm, p, num_seqs, max_seqlen_q, s);
+}
+
+extern "C" int nvattn_tree_verify(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                                  const void* k_cache, const void* v_cache, void* out,
+                                  int64_t o_stride_tok, int64_t o_stride_head,
+                                  const int32_t* cu_seqlens_q, const int32_t* context_lens,
+                                  const uint64_t* tree_mask, const int32_t* block_table,
+                                  int64_t block_table_stride, int32_t max_blocks_per_seq,
+                                  int32_t num_blocks, int32_t block_size, int32_t num_seqs,
+                                  int32_t max_nodes, int64_t total_q, int32_t num_heads,
+                                  int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
+                                  int32_t* status, void* stream) {
+  clear_error();
+  if (num_seqs < 0 || total_q < 0 || max_nodes < 0)
+    return fail(NVATTN_ERR_INVALID, "tree_verify: negative size");
+  if (num_seqs == 0 || total_q == 0 || max_nodes == 0) return NVATTN_OK;
+  if (max_nodes > 64) return fail(NVATTN_ERR_UNSUPPORTED, "tree_verify: at most 64 tree nodes");
+  int rc = tc_check_q_out(q, q_stride_tok, q_stride_head, out, o_stride_tok, o_stride_head,
+                          num_heads, num_kv_heads, head_dim, "tree_verify");
+  if (rc) return rc;
+  if (!k_cache || !v_cache || !cu_seqlens_q || !context_lens || !tree_mask || !block_table)
+    return fail(NVATTN_ERR_INVALID, "tree_verify: NULL pointer");
+  if (block_size <= 0 || block_size % tc::kBN)
+    return fail(NVATTN_ERR_UNSUPPORTED, "tree_verify: block_size must be a multiple of 128");
+  if (num_blocks <= 0 || max_blocks_per_seq <= 0 || block_table_stride < max_blocks_per_seq)
+    return fail(NVATTN_ERR_INVALID, "tree_verify: bad block table geometry");
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(NVATTN_ERR_INVALID, "tree_verify: caches must be 16-byte aligned");
+  tc::Params p = tc_params(out, o_stride_tok, o_stride_head, num_heads, num_kv_heads,
+                           softmax_scale, total_q, status);
+  CUtensorMap qm, km, vm;
+  rc = tc::make_q_map(&qm, q, total_q, num_heads, q_stride_tok, q_stride_head, p.group, p.tpt);
+  if (rc) return rc;
+  rc = tc::make_kv_map(&km, k_cache, true, 0, num_blocks, block_size, num_kv_heads, 0, 0);
+  if (rc) return rc;
+  rc = tc::make_kv_map(&vm, v_cache, true, 0, num_blocks, block_size, num_kv_heads, 0, 0);
+  if (rc) return rc;
+  p.cu_q = cu_seqlens_q;
+  p.ctx_lens = context_lens;
+  p.tree_mask = tree_mask;
+  p.block_table = block_table;
+  p.bt_stride = block_table_stride;
+  p.max_blocks = max_blocks_per_seq;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.causal = 1;
+  return tc::launch<tc::kTree>(qm, km, vm, p, num_seqs, max_nodes,
+                               reinterpret_cast<cudaStream_t>(stream));
+}
