@@ -560,6 +560,23 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_only(args):
+    """One secondary workload alone (used to profile its kernel)."""
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    hbm_peak, tf_peak, _, _ = load_peaks()
+    if args.only == "prefill":
+        res = bench_prefill(dev, rank, world, args, tf_peak)
+    else:
+        res = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -570,12 +587,16 @@ def main():
                     help="decode batch (configs[3] = 128; smaller values only for ncu captures)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
+    ap.add_argument("--only", choices=("prefill", "tree"), default=None,
+                    help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args)
     else:
         run_nvattn(args)
 

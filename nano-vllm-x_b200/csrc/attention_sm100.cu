@@ -82,8 +82,10 @@ struct Params {
 
 struct Barriers {
   uint64_t q_full;
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t o_done;
@@ -168,8 +170,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
@@ -203,41 +207,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int32_t* bt =
           (MODE == kDense) ? nullptr : p.block_table + static_cast<int64_t>(b) * p.bt_stride;
       int issued = 0;
-      for (int j = 0; j < ntiles; ++j) {
+      bool ok = true;
+      for (int j = 0; ok && j < ntiles; ++j) {
         const int st = j % kStages;
-        if (!mbar_wait(&bars->kv_empty[st], ((j / kStages) & 1) ^ 1)) {
-          set_status(p.status, NVATTN_STATUS_TIMEOUT);
-          break;
-        }
+        const uint32_t par = ((j / kStages) & 1) ^ 1;
         const int j0 = j * kBN;
         uint8_t* kd = smem + kQBytes + st * 2 * kOperand;
         uint8_t* vd = kd + kOperand;
-        mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kOperand);
+        int c2 = 0, c3 = 0;  // token coordinate / block coordinate of the tile
         if (MODE == kDense) {
-          const int row = k_begin + j0;
-          tma_load_3d(kd, &kmap, &bars->kv_full[st], 0, g, row);
-          tma_load_3d(kd + kHalf, &kmap, &bars->kv_full[st], 64, g, row);
-          tma_load_3d(vd, &vmap, &bars->kv_full[st], 0, g, row);
-          tma_load_3d(vd + kHalf, &vmap, &bars->kv_full[st], 64, g, row);
+          c2 = k_begin + j0;
         } else {
           int blk = bt[j0 / p.block_size];
           if (blk < 0 || blk >= p.num_blocks) {
             set_status(p.status, NVATTN_STATUS_BAD_BLOCK);
             blk = 0;
           }
-          const int tin = j0 % p.block_size;
-          tma_load_4d(kd, &kmap, &bars->kv_full[st], 0, g, tin, blk);
-          tma_load_4d(kd + kHalf, &kmap, &bars->kv_full[st], 64, g, tin, blk);
-          tma_load_4d(vd, &vmap, &bars->kv_full[st], 0, g, tin, blk);
-          tma_load_4d(vd + kHalf, &vmap, &bars->kv_full[st], 64, g, tin, blk);
+          c2 = j0 % p.block_size;
+          c3 = blk;
+        }
+        // K ring slot frees after S1 of the tile two back; V after its PV1.
+        if (!mbar_wait(&bars->k_empty[st], par)) { ok = false; break; }
+        mbar_arrive_expect_tx(&bars->k_full[st], kOperand);
+        if (MODE == kDense) {
+          tma_load_3d(kd, &kmap, &bars->k_full[st], 0, g, c2);
+          tma_load_3d(kd + kHalf, &kmap, &bars->k_full[st], 64, g, c2);
+        } else {
+          tma_load_4d(kd, &kmap, &bars->k_full[st], 0, g, c2, c3);
+          tma_load_4d(kd + kHalf, &kmap, &bars->k_full[st], 64, g, c2, c3);
+        }
+        if (!mbar_wait(&bars->v_empty[st], par)) { ok = false; issued = -(j + 1); break; }
+        mbar_arrive_expect_tx(&bars->v_full[st], kOperand);
+        if (MODE == kDense) {
+          tma_load_3d(vd, &vmap, &bars->v_full[st], 0, g, c2);
+          tma_load_3d(vd + kHalf, &vmap, &bars->v_full[st], 64, g, c2);
+        } else {
+          tma_load_4d(vd, &vmap, &bars->v_full[st], 0, g, c2, c3);
+          tma_load_4d(vd + kHalf, &vmap, &bars->v_full[st], 64, g, c2, c3);
         }
         issued = j + 1;
       }
+      if (!ok) set_status(p.status, NVATTN_STATUS_TIMEOUT);
       // Drain: no copy of ours may still be in flight when the CTA ends. The
       // last use of each ring slot is the last phase that barrier completes.
       mbar_wait(&bars->q_full, 0);
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        mbar_wait(&bars->kv_full[j % kStages], (j / kStages) & 1);
+      const int k_issued = issued < 0 ? -issued : issued;  // K of tile |issued|-1 went out
+      const int v_issued = issued < 0 ? -issued - 1 : issued;
+      for (int j = max(0, k_issued - kStages); j < k_issued; ++j)
+        mbar_wait(&bars->k_full[j % kStages], (j / kStages) & 1);
+      for (int j = max(0, v_issued - kStages); j < v_issued; ++j)
+        mbar_wait(&bars->v_full[j % kStages], (j / kStages) & 1);
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
@@ -258,22 +277,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           sm100::mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, vdesc(v_s(st), kk), idesc_o,
                         (j > 0 || kk > 0) ? 1u : 0u);
       };
-      if (ok) ok = mbar_wait(&bars->kv_full[0], 0);
+      if (ok) ok = mbar_wait(&bars->k_full[0], 0);
       if (ok) {
         sm100::fence_after_sync();
         issue_s(0, 0);
         issue_s(1, 0);
+        sm100::commit(&bars->k_empty[0]);
       }
       for (int j = 0; ok && j < ntiles; ++j) {
         const int st = j % kStages;
         const int nst = (j + 1) % kStages;
         const bool more = j + 1 < ntiles;
-        ok = mbar_wait(&bars->p_full[0], j & 1);
+        ok = mbar_wait(&bars->p_full[0], j & 1) && mbar_wait(&bars->v_full[st], (j / kStages) & 1);
         if (!ok) break;
         sm100::fence_after_sync();
         issue_pv(0, st, j);
         if (more) {
-          ok = mbar_wait(&bars->kv_full[nst], ((j + 1) / kStages) & 1);
+          ok = mbar_wait(&bars->k_full[nst], ((j + 1) / kStages) & 1);
           if (!ok) break;
           sm100::fence_after_sync();
           issue_s(0, nst);
@@ -282,8 +302,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         sm100::fence_after_sync();
         issue_pv(1, st, j);
-        sm100::commit(&bars->kv_empty[st]);
-        if (more) issue_s(1, nst);
+        sm100::commit(&bars->v_empty[st]);
+        if (more) {
+          issue_s(1, nst);
+          sm100::commit(&bars->k_empty[nst]);
+        }
       }
       if (!ok) set_status(p.status, NVATTN_STATUS_TIMEOUT);
       // All MMAs done -> O final; also makes sure none is in flight at exit.
@@ -316,9 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm100::fence_after_sync();
       const int j0 = j * kBN;
       const bool full_row = j0 + kBN <= mask_from;  // no key of this tile is masked
-      // Scaled (and masked) score of column e of a 32-column chunk.
-      auto score = [&](uint32_t raw, int key) -> float {
-        const float x = __uint_as_float(raw) * p.scale_log2;
+      // Raw score or -inf where masked (scale is applied later: it is > 0).
+      auto masked = [&](uint32_t raw, int key) -> float {
+        const float x = __uint_as_float(raw);
         if (full_row) return x;
         bool okk;
         if (MODE == kTree) {
@@ -329,16 +352,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return okk ? x : -INFINITY;
       };
-      // Pass 1: row max over the tile (32 columns in registers at a time).
-      float mx = -INFINITY;
+      // Pass 1: row max of the raw scores, 64 columns per TMEM round trip.
+      float mraw = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        sm100::tmem_ld32(t_lane + col_s(wg) + c * 32, sr);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sr[64];
+        sm100::tmem_ld32(t_lane + col_s(wg) + h * 64, sr);
+        sm100::tmem_ld32(t_lane + col_s(wg) + h * 64 + 32, sr + 32);
         sm100::tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, score(sr[e], j0 + c * 32 + e));
+        for (int e = 0; e < 64; ++e) mraw = fmaxf(mraw, masked(sr[e], j0 + h * 64 + e));
       }
+      const float mx = (mraw == -INFINITY) ? -INFINITY : mraw * p.scale_log2;
       // Lazy rescale: keep the reference max unless the row max grew by > 2^8.
       float alpha = 1.f;
       bool need = false;
@@ -349,26 +374,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
       }
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
-      // Pass 2: P = exp2(score - base) as bf16 pairs, written over S. Chunk c
-      // of S (columns 32c..32c+31) becomes P columns 16c..16c+15; chunk c is
-      // read before any store can reach its columns.
-      float sum = 0.f;
+      // Pass 2: P = exp2(raw*scale - base) two columns per packed fp32x2 FMA,
+      // written over S as bf16 pairs. Columns 64h..64h+63 of S become P
+      // columns 32h..32h+31, which only overlap S columns already read.
+      const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
+      const uint64_t nbase2 = pack_f32x2(-base, -base);
+      uint64_t sum2 = pack_f32x2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        sm100::tmem_ld32(t_lane + col_s(wg) + c * 32, sr);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sr[64];
+        sm100::tmem_ld32(t_lane + col_s(wg) + h * 64, sr);
+        sm100::tmem_ld32(t_lane + col_s(wg) + h * 64 + 32, sr + 32);
         sm100::tmem_wait_ld();
-        uint32_t pk[16];
+        uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(score(sr[2 * e], j0 + c * 32 + 2 * e) - base);
-          const float p1 = fast_exp2(score(sr[2 * e + 1], j0 + c * 32 + 2 * e + 1) - base);
-          sum += p0 + p1;
+        for (int e = 0; e < 32; ++e) {
+          const int key = j0 + h * 64 + 2 * e;
+          const uint64_t x2 = fma_f32x2(
+              pack_f32x2(masked(sr[2 * e], key), masked(sr[2 * e + 1], key + 1)), scale2, nbase2);
+          const float2 x = unpack_f32x2(x2);
+          const float p0 = fast_exp2(x.x), p1 = fast_exp2(x.y);
+          sum2 = add_f32x2(sum2, pack_f32x2(p0, p1));
           pk[e] = pack_bf16x2(p0, p1);
         }
-        sm100::tmem_st16(t_lane + col_s(wg) + c * 16, pk);
+        sm100::tmem_st32(t_lane + col_s(wg) + h * 32, pk);
       }
-      l += sum;
+      {
+        const float2 sm = unpack_f32x2(sum2);
+        l += sm.x + sm.y;
+      }
       // O rescale after P is out of registers (keeps the score row and this
       // buffer from being live together).
       if (j > 0 && __any_sync(0xffffffffu, need)) {
