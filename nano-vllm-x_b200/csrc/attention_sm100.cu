@@ -58,6 +58,7 @@ constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int i) { return static_cast<uint32_t>(i) * 128u; }
 __device__ __forceinline__ uint32_t col_o(int i) { return 256u + static_cast<uint32_t>(i) * 128u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
+constexpr int kPolyEvery = 4;  // lean tiles: 1 exp2 pair in 4 from the FMA-pipe polynomial
 
 enum Mode { kDense = 0, kPaged = 1, kTree = 2 };
 
@@ -342,7 +343,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Raw score or -inf where masked (scale is applied later: it is > 0).
       auto masked = [&](uint32_t raw, int key) -> float {
         const float x = __uint_as_float(raw);
-        if (full_row) return x;
         bool okk;
         if (MODE == kTree) {
           const int t = key - ctx;
@@ -352,6 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return okk ? x : -INFINITY;
       };
+      // Tiles where no row of the warp is masked take the lean path.
+      const bool wfull = __all_sync(0xffffffffu, full_row);
       // Pass 1: row max of the raw scores, 64 columns per TMEM round trip.
       float mraw = -INFINITY;
 #pragma unroll
@@ -360,8 +362,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tmem_ld32(t_lane + col_s(wg) + h * 64, sr);
         sm100::tmem_ld32(t_lane + col_s(wg) + h * 64 + 32, sr + 32);
         sm100::tmem_wait_ld();
+        if (wfull) {
 #pragma unroll
-        for (int e = 0; e < 64; ++e) mraw = fmaxf(mraw, masked(sr[e], j0 + h * 64 + e));
+          for (int e = 0; e < 64; e += 2)
+            mraw = fmax3(mraw, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; e += 2)
+            mraw = fmax3(mraw, masked(sr[e], j0 + h * 64 + e),
+                         masked(sr[e + 1], j0 + h * 64 + e + 1));
+        }
       }
       const float mx = (mraw == -INFINITY) ? -INFINITY : mraw * p.scale_log2;
       // Lazy rescale: keep the reference max unless the row max grew by > 2^8.
@@ -374,9 +384,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
       }
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
-      // Pass 2: P = exp2(raw*scale - base) two columns per packed fp32x2 FMA,
+      // Pass 2: P = exp2(raw*scale - base), two columns per packed fp32x2 FMA,
       // written over S as bf16 pairs. Columns 64h..64h+63 of S become P
       // columns 32h..32h+31, which only overlap S columns already read.
+      // In lean tiles one pair in kPolyEvery takes exp2 from a polynomial on
+      // the FMA pipe instead of the MUFU unit, which both softmax warpgroups
+      // of a sub-partition share.
       const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
       const uint64_t nbase2 = pack_f32x2(-base, -base);
       uint64_t sum2 = pack_f32x2(0.f, 0.f);
@@ -387,15 +400,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tmem_ld32(t_lane + col_s(wg) + h * 64 + 32, sr + 32);
         sm100::tmem_wait_ld();
         uint32_t pk[32];
+        if (wfull) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = j0 + h * 64 + 2 * e;
-          const uint64_t x2 = fma_f32x2(
-              pack_f32x2(masked(sr[2 * e], key), masked(sr[2 * e + 1], key + 1)), scale2, nbase2);
-          const float2 x = unpack_f32x2(x2);
-          const float p0 = fast_exp2(x.x), p1 = fast_exp2(x.y);
-          sum2 = add_f32x2(sum2, pack_f32x2(p0, p1));
-          pk[e] = pack_bf16x2(p0, p1);
+          for (int e = 0; e < 32; ++e) {
+            const uint64_t x2 = fma_f32x2((static_cast<uint64_t>(sr[2 * e + 1]) << 32) | sr[2 * e],
+                                          scale2, nbase2);
+            const uint64_t p2 = (e % kPolyEvery == kPolyEvery - 1) ? exp2_poly_f32x2(x2)
+                                                                    : exp2_mufu_f32x2(x2);
+            sum2 = add_f32x2(sum2, p2);
+            const float2 pp = unpack_f32x2(p2);
+            pk[e] = pack_bf16x2(pp.x, pp.y);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = j0 + h * 64 + 2 * e;
+            const uint64_t x2 = fma_f32x2(
+                pack_f32x2(masked(sr[2 * e], key), masked(sr[2 * e + 1], key + 1)), scale2,
+                nbase2);
+            const uint64_t p2 = exp2_mufu_f32x2(x2);
+            sum2 = add_f32x2(sum2, p2);
+            const float2 pp = unpack_f32x2(p2);
+            pk[e] = pack_bf16x2(pp.x, pp.y);
+          }
         }
         sm100::tmem_st32(t_lane + col_s(wg) + h * 32, pk);
       }

@@ -182,6 +182,42 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// exp2 of both lanes on the MUFU unit (ex2.approx: exact 0 for -inf).
+__device__ __forceinline__ uint64_t exp2_mufu_f32x2(uint64_t x2) {
+  const float2 x = unpack_f32x2(x2);
+  return pack_f32x2(fast_exp2(x.x), fast_exp2(x.y));
+}
+
+// exp2 of both lanes on the FMA pipe, for finite inputs. Cody-Waite split
+// x = n + f with n = round(x) (adding 1.5*2^23 leaves n in the low mantissa
+// bits), f in [-0.5, 0.5]; 2^f from a cubic fitted here to relative error
+// 7.5e-5 (near-minimax: Lawson-weighted least squares on Chebyshev nodes),
+// then n is added to the exponent field. Inputs are clamped to >= -127
+// (result ~6e-39, i.e. zero for a softmax sum that is >= 2^-8).
+__device__ __forceinline__ uint64_t exp2_poly_f32x2(uint64_t x2) {
+  float2 x = unpack_f32x2(x2);
+  x.x = fmaxf(x.x, -127.f);
+  x.y = fmaxf(x.y, -127.f);
+  const uint64_t xc = pack_f32x2(x.x, x.y);
+  const uint64_t t = add_f32x2(xc, pack_f32x2(12582912.f, 12582912.f));
+  const uint64_t n = add_f32x2(t, pack_f32x2(-12582912.f, -12582912.f));
+  const uint64_t f = fma_f32x2(n, pack_f32x2(-1.f, -1.f), xc);
+  uint64_t q = fma_f32x2(pack_f32x2(0.0551716648f, 0.0551716648f), f,
+                         pack_f32x2(0.2426111251f, 0.2426111251f));
+  q = fma_f32x2(q, f, pack_f32x2(0.6932609677f, 0.6932609677f));
+  q = fma_f32x2(q, f, pack_f32x2(0.9999280572f, 0.9999280572f));
+  const uint32_t tlo = static_cast<uint32_t>(t), thi = static_cast<uint32_t>(t >> 32);
+  const uint32_t qlo = static_cast<uint32_t>(q) + (tlo << 23);
+  const uint32_t qhi = static_cast<uint32_t>(q >> 32) + (thi << 23);
+  return (static_cast<uint64_t>(qhi) << 32) | qlo;
+}
+
 // Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` inside a tile
 // whose rows are 128 bytes and that TMA wrote with CU_TENSOR_MAP_SWIZZLE_128B
 // (tile base 1024-byte aligned).
