@@ -541,21 +541,25 @@ int make_q_map(CUtensorMap* map, const void* q, int64_t total_q, int num_heads, 
 
 constexpr int kSmemBytes = kSmemData + 1024 + static_cast<int>(sizeof(Barriers)) + 64;
 
+// Per (mode, device): the kernel's dynamic shared-memory limit has been
+// raised. File scope (internal linkage), so every copy of the library keeps
+// its own flags.
+static std::mutex g_attr_mu;
+static bool g_attr_done[3][64];
+
 template <int MODE>
 int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const Params& p,
            int num_seqs, int max_tokens, cudaStream_t stream) {
-  static std::mutex mu;
-  static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   {
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev >= 64 || !attr_done[dev]) {
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    if (dev >= 64 || !g_attr_done[MODE][dev]) {
       cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<MODE>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            kSmemBytes);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tc_kernel)");
-      if (dev < 64) attr_done[dev] = true;
+      if (dev < 64) g_attr_done[MODE][dev] = true;
     }
   }
   const int blocks_m = (max_tokens + 2 * p.tpt - 1) / (2 * p.tpt);
