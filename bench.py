@@ -177,20 +177,22 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(x: float, world: int) -> float:
+def max_over_ranks(x: float, world: int, device: str = "cuda") -> float:
+    """Job time = the slowest rank's time (every rank calls this, same order)."""
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
 
-def sum_over_ranks(x: float, world: int) -> float:
+def sum_over_ranks(x: float, world: int, device: str = "cuda") -> float:
+    """Whole-job work = the sum of every rank's work."""
     if world == 1:
         return x
     import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
 

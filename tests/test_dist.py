@@ -1,0 +1,98 @@
+"""Multi-rank host logic on CPU (gloo, world size 2).
+
+The attention path shards by head across tensor-parallel ranks with no
+collective inside attention (qwen3.py:29-35, model_runner.py:110). These
+tests run two gloo ranks on the CPU: each rank computes the oracle on its own
+head shard (nvattn.parallel.head_shard), the shards are gathered, and the
+result must equal the unsharded computation; the bench's max-over-ranks /
+sum-over-ranks reductions are checked the same way.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import REPO  # noqa: F401  (sets import paths)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q, result_q):
+    import sys
+    for p in q["paths"]:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from nvattn.parallel import head_shard
+        from oracle import reference_math as R
+        import bench
+        (q0, q1), (k0, k1) = head_shard(q["H"], q["KVH"], rank, world)
+        # decode on this rank's shard of the paged cache
+        out = R.decode_attention(q["q"][:, q0:q1], q["kc"][:, :, k0:k1], q["vc"][:, :, k0:k1],
+                                 q["lens"], q["bt"], 128 ** -0.5)
+        parts = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(parts, out)
+        # prefill on the shard (dense varlen)
+        pf = R.varlen_attention(q["pq"][:, q0:q1], q["pk"][:, k0:k1], q["pv"][:, k0:k1],
+                                q["cu"], q["cu"], 128 ** -0.5, True)
+        pparts = [torch.empty_like(pf) for _ in range(world)]
+        dist.all_gather(pparts, pf)
+        mx = bench.max_over_ranks(float(rank + 1), world, device="cpu")
+        sm = bench.sum_over_ranks(float(rank + 1), world, device="cpu")
+        if rank == 0:
+            result_q.put((torch.cat(parts, dim=1).numpy(), torch.cat(pparts, dim=1).numpy(), mx, sm))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_head_sharded_attention_equals_unsharded_world2():
+    g = torch.Generator().manual_seed(0)
+    H, KVH, BS = 16, 8, 256
+    lens = np.array([5, 300, 700], np.int32)
+    nblk = (lens + BS - 1) // BS
+    bt = np.full((3, int(nblk.max())), -1, np.int32)
+    pos = 0
+    for b, n in enumerate(nblk):
+        bt[b, :n] = np.arange(pos, pos + n)
+        pos += n
+    kc = torch.randn(pos, BS, KVH, 128, generator=g).bfloat16()
+    vc = torch.randn(pos, BS, KVH, 128, generator=g).bfloat16()
+    q = torch.randn(3, H, 128, generator=g).bfloat16()
+    plens = [7, 40]
+    cu = np.concatenate([[0], np.cumsum(plens)]).astype(np.int32)
+    pq = torch.randn(47, H, 128, generator=g).bfloat16()
+    pk = torch.randn(47, KVH, 128, generator=g).bfloat16()
+    pv = torch.randn(47, KVH, 128, generator=g).bfloat16()
+    from conftest import GOLDEN, PROJECT
+    payload = dict(H=H, KVH=KVH, q=q, kc=kc, vc=vc, lens=lens, bt=bt, pq=pq, pk=pk, pv=pv, cu=cu,
+                   paths=[str(REPO), str(PROJECT), str(GOLDEN)])
+    ctx = mp.get_context("spawn")
+    result_q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, payload, result_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    dec, pre, mx, sm = result_q.get()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    dec, pre = torch.from_numpy(dec), torch.from_numpy(pre)
+    from oracle import reference_math as R
+    full_dec = R.decode_attention(q, kc, vc, lens, bt, 128 ** -0.5)
+    full_pre = R.varlen_attention(pq, pk, pv, cu, cu, 128 ** -0.5, True)
+    assert torch.allclose(dec, full_dec, atol=1e-6)
+    assert torch.allclose(pre, full_pre, atol=1e-6)
+    assert mx == 2.0 and sm == 3.0
