@@ -20,6 +20,6 @@ __all__ = [
 
 
 def install() -> None:
-    """Replace Nano-vLLM-X's Attention with nvattn's (see nvattn.install)."""
-    from .install import install as _install
+    """Replace Nano-vLLM-X's Attention with nvattn's (see nvattn._engine_hook)."""
+    from ._engine_hook import install as _install
     _install()

@@ -55,6 +55,8 @@ SIGNATURES: dict[str, tuple] = {
                                             _I32P, _I32P, c_int64, c_int32, c_int32, c_int32,
                                             c_int32, c_int32, c_int32, c_int32, c_float, _I32P,
                                             _P]),
+    "nvattn_tree_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int64, c_int32, c_int32,
+                                               c_int32, c_int32]),
     "nvattn_tree_verify": (c_int, [_P, c_int64, c_int64,
                                    _P, _P,
                                    _P, c_int64, c_int64,
@@ -62,7 +64,7 @@ SIGNATURES: dict[str, tuple] = {
                                    _I32P, c_int64, c_int32, c_int32, c_int32,
                                    c_int32, c_int32, c_int64,
                                    c_int32, c_int32, c_int32,
-                                   c_float, _I32P, _P]),
+                                   c_float, _P, c_size_t, _I32P, _P]),
     "nvattn_kv_move": (c_int, [_P, _P, _I32P, _I32P, _I32P, c_int32, c_int32, c_int64, c_int64,
                                _I32P, _P]),
 }

@@ -1,0 +1,223 @@
+"""End-to-end generation through the reference engine with nvattn attention.
+
+the reference's own engine (Nano-vLLM-X: LLM ->
+LLMEngine -> Scheduler/BlockManager -> ModelRunner with CUDA-graph decode)
+generates for bench.py's workload (random.seed(0); 256 requests of random
+token ids, input and output lengths uniform in [100, 1024], ignore_eos;
+bench.py:8-24) with a random-init Qwen3-0.6B: 28 layers, hidden 1024,
+16 Q / 8 KV heads, head_dim 128, vocab 151936, RMSNorm, RoPE theta 1e6,
+bf16. Greedy decoding.
+
+The engine is used unchanged except for what this environment lacks:
+
+* weights: seeded random bf16 tensors written as safetensors next to a
+  written config.json (no checkpoint is available offline);
+* tokenizer: the workload is token ids only, so AutoTokenizer is replaced
+  by a stub (no tokenizer files are available);
+* sampler: the reference forbids temperature 0 (sampling_params.py:11) and
+  samples stochastically (sampler.py:11); greedy decoding takes the argmax
+  of the same logits;
+* attention: ``--attn nvattn`` swaps nanovllm.layers.attention.Attention for
+  nvattn.Attention in every engine process (tensor-parallel workers are
+  spawned, so the swap runs in ModelRunner's constructor); ``--attn
+  reference`` keeps the engine's own flash-attn / Triton path.
+
+    python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz]
+
+Prints one JSON line: output tokens, seconds, tok/s. Needs the reference
+package importable (e.g. ``pip install --no-deps --target baseline/_ref``).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+QWEN3_0_6B = dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                  num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                  vocab_size=151936, max_position_embeddings=40960, rms_norm_eps=1e-6,
+                  rope_theta=1000000.0, tie_word_embeddings=True, hidden_act="silu",
+                  attention_bias=False, dtype="bfloat16")
+
+
+def write_model(path: Path, seed: int = 0, **overrides) -> None:
+    """config.json + seeded random weights (HF parameter names) as safetensors."""
+    from safetensors.torch import save_file
+    from transformers import Qwen3Config
+
+    cfg = dict(QWEN3_0_6B, **overrides)
+    Qwen3Config(**cfg).save_pretrained(path)
+    g = torch.Generator().manual_seed(seed)
+    h, inter, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"]
+    nh, nkv, d, V = (cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"],
+                     cfg["vocab_size"])
+
+    def w(*shape, std=0.02):
+        return (torch.randn(*shape, generator=g) * std).to(torch.bfloat16)
+
+    def norm(n):
+        return (1.0 + 0.1 * torch.randn(n, generator=g)).to(torch.bfloat16)
+
+    tensors = {"model.embed_tokens.weight": w(V, h), "model.norm.weight": norm(h)}
+    for i in range(L):
+        p = f"model.layers.{i}."
+        tensors.update({
+            p + "input_layernorm.weight": norm(h),
+            p + "post_attention_layernorm.weight": norm(h),
+            p + "self_attn.q_proj.weight": w(nh * d, h),
+            p + "self_attn.k_proj.weight": w(nkv * d, h),
+            p + "self_attn.v_proj.weight": w(nkv * d, h),
+            p + "self_attn.o_proj.weight": w(h, nh * d),
+            p + "self_attn.q_norm.weight": norm(d),
+            p + "self_attn.k_norm.weight": norm(d),
+            p + "mlp.gate_proj.weight": w(inter, h),
+            p + "mlp.up_proj.weight": w(inter, h),
+            p + "mlp.down_proj.weight": w(h, inter),
+        })
+    save_file(tensors, str(path / "model.safetensors"))
+
+
+class _TokenizerStub:
+    """Token-id workloads need no tokenizer; decode() is only used for text."""
+
+    eos_token_id = -1
+
+    @classmethod
+    def from_pretrained(cls, *args, **kwargs):
+        return cls()
+
+    def encode(self, text):
+        raise ValueError("the e2e harness takes token-id prompts only")
+
+    def decode(self, token_ids):
+        return ""
+
+
+def _greedy_forward(self, logits, temperatures):
+    return logits.float().argmax(dim=-1)
+
+
+def patch_engine(attn: str) -> None:
+    """Apply the substitutions listed in the module docstring (idempotent)."""
+    import nanovllm.engine.llm_engine as llm_engine
+    import nanovllm.engine.model_runner as model_runner
+    import nanovllm.layers.sampler as sampler
+
+    sampler.Sampler.forward = _greedy_forward
+    model_runner.Sampler = sampler.Sampler
+    llm_engine.AutoTokenizer = _TokenizerStub
+    llm_engine.ModelRunner = E2EModelRunner
+    if attn == "nvattn":
+        import nvattn
+        nvattn.install()
+
+
+def _runner_base():
+    import nanovllm.engine.model_runner as model_runner
+    return model_runner.ModelRunner
+
+
+def _make_runner_class():
+    base = _runner_base()
+
+    class Runner(base):
+        """ModelRunner that re-applies the substitutions in its own process
+        (tensor-parallel workers are started with the spawn method)."""
+
+        def __init__(self, config, rank, event):
+            patch_engine(os.environ.get("NVATTN_E2E_ATTN", "nvattn"))
+            super().__init__(config, rank, event)
+
+    Runner.__module__ = __name__
+    Runner.__qualname__ = "E2EModelRunner"
+    return Runner
+
+
+def __getattr__(name):  # module-level lazy class (needs the reference importable)
+    if name == "E2EModelRunner":
+        cls = _make_runner_class()
+        globals()["E2EModelRunner"] = cls
+        return cls
+    raise AttributeError(name)
+
+
+def bench_workload(num_seqs: int = 256, max_input_len: int = 1024, max_output_len: int = 1024):
+    """bench.py's draw order under random.seed(0) (bench.py:8-14)."""
+    random.seed(0)
+    prompts = [[random.randint(0, 10000) for _ in range(random.randint(100, max_input_len))]
+               for _ in range(num_seqs)]
+    max_tokens = [random.randint(100, max_output_len) for _ in range(num_seqs)]
+    return prompts, max_tokens
+
+
+def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: int,
+        enforce_eager: bool, model_dir: str | None = None, out: str | None = None) -> dict:
+    os.environ["NVATTN_E2E_ATTN"] = attn
+    import nanovllm.engine.llm_engine as llm_engine  # noqa: F401  (reference)
+    global E2EModelRunner
+    E2EModelRunner = _make_runner_class()
+    patch_engine(attn)
+    from nanovllm import LLM, SamplingParams
+
+    tmp = None
+    if model_dir is None:
+        tmp = tempfile.TemporaryDirectory()
+        model_dir = tmp.name
+        write_model(Path(model_dir))
+    prompts, max_tokens = bench_workload(num_seqs, max_input_len, max_output_len)
+    llm = LLM(model_dir, enforce_eager=enforce_eager, max_model_len=4096, tensor_parallel_size=tp)
+    sps = [SamplingParams(temperature=1.0, ignore_eos=True, max_tokens=m) for m in max_tokens]
+    llm.generate([[1, 2, 3]], SamplingParams(max_tokens=4), use_tqdm=False)  # warm-up
+    torch.cuda.synchronize()
+    t = time.time()
+    outs = llm.generate(prompts, sps, use_tqdm=False)
+    dt = time.time() - t
+    total = sum(max_tokens)
+    res = {"metric": "e2e out tok/s", "attn": attn, "tp": tp, "num_seqs": num_seqs,
+           "output_tokens": total, "seconds": round(dt, 3), "value": round(total / dt, 1),
+           "unit": "tok/s", "enforce_eager": enforce_eager,
+           "model": "random-init Qwen3-0.6B (28 layers, 16Q/8KV, d128, vocab 151936, bf16)",
+           "decoding": "greedy"}
+    if out:
+        np.savez_compressed(out, **{f"r{i}": np.array(o["token_ids"], np.int32)
+                                    for i, o in enumerate(outs)})
+    # Stop the engine's workers now (its atexit hook would do the same later).
+    import atexit
+    atexit.unregister(llm.exit)
+    llm.exit()
+    if tmp is not None:
+        tmp.cleanup()
+    return res
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--attn", choices=("nvattn", "reference"), default="nvattn")
+    ap.add_argument("--num-seqs", type=int, default=256)
+    ap.add_argument("--max-input-len", type=int, default=1024)
+    ap.add_argument("--max-output-len", type=int, default=1024)
+    ap.add_argument("--enforce-eager", action="store_true")
+    ap.add_argument("--model-dir", default=None, help="reuse a written model directory")
+    ap.add_argument("--write-model", default=None, help="only write the model to this dir")
+    ap.add_argument("--out", default=None, help="save generated token ids (npz)")
+    args = ap.parse_args()
+    if args.write_model:
+        Path(args.write_model).mkdir(parents=True, exist_ok=True)
+        write_model(Path(args.write_model))
+        return
+    res = run(args.tp, args.attn, args.num_seqs, args.max_input_len, args.max_output_len,
+              args.enforce_eager, args.model_dir, args.out)
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

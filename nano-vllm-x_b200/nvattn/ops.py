@@ -32,6 +32,7 @@ __all__ = [
     "tree_attention",
     "kv_move",
     "decode_workspace_bytes",
+    "tree_workspace_bytes",
     "status_tensor",
     "read_status",
 ]
@@ -74,7 +75,10 @@ def status_tensor(device: torch.device | int | None = None) -> torch.Tensor | No
     if t is None:
         if torch.cuda.is_current_stream_capturing():
             return None
-        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        # a normal tensor even when first used under torch.inference_mode(),
+        # so read_status() can clear it anywhere
+        with torch.inference_mode(False):
+            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _status[idx] = t
     return t
 
@@ -297,11 +301,17 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens=None, block_table
 
 # ------------------------------------------------------------------------ tree
 
+def tree_workspace_bytes(num_seqs: int, max_nodes: int, total_q: int, num_heads: int,
+                         num_kv_heads: int, max_blocks: int, block_size: int) -> int:
+    return int(_lib.load().nvattn_tree_workspace_bytes(num_seqs, max_nodes, total_q, num_heads,
+                                                       num_kv_heads, max_blocks, block_size))
+
+
 def tree_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                    cu_seqlens_q: torch.Tensor, context_lens: torch.Tensor,
                    tree_mask: torch.Tensor, block_table: torch.Tensor, max_nodes: int,
-                   softmax_scale: float | None = None,
-                   out: torch.Tensor | None = None) -> torch.Tensor:
+                   softmax_scale: float | None = None, out: torch.Tensor | None = None,
+                   workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Draft-tree verification attention.
 
     q: (total_nodes, H, d); sequence b's nodes are rows cu_seqlens_q[b]..;
@@ -330,12 +340,17 @@ def tree_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor
         softmax_scale = head_dim ** -0.5
     if out is None:
         out = torch.empty((total_q, num_heads, head_dim), dtype=q.dtype, device=q.device)
+    ws_bytes = tree_workspace_bytes(num_seqs, int(max_nodes), total_q, num_heads, num_kv_heads,
+                                    block_table.shape[1], block_size)
+    if ws_bytes and (workspace is None or workspace.numel() * workspace.element_size() < ws_bytes):
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if (ws_bytes and workspace is not None) else None
     _lib.call("nvattn_tree_verify", q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(),
               v_cache.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1),
               cu_seqlens_q.data_ptr(), context_lens.data_ptr(), tree_mask.data_ptr(),
               block_table.data_ptr(), block_table.stride(0), block_table.shape[1], num_blocks,
               block_size, num_seqs, int(max_nodes), total_q, num_heads, num_kv_heads, head_dim,
-              float(softmax_scale), _status_ptr(dev), _stream(dev))
+              float(softmax_scale), ws_ptr, ws_bytes, _status_ptr(dev), _stream(dev))
     return out
 
 

@@ -19,6 +19,11 @@ GOLDEN = REPO / "tests" / "golden"
 for p in (str(REPO), str(PROJECT), str(GOLDEN)):
     if p not in sys.path:
         sys.path.insert(0, p)
+# The reference engine, when installed next to the repo (pip --target
+# baseline/_ref), for the tests that drive nvattn from inside it.
+REF_INSTALL = REPO / "baseline" / "_ref"
+if REF_INSTALL.is_dir() and str(REF_INSTALL) not in sys.path:
+    sys.path.append(str(REF_INSTALL))
 
 
 def pytest_configure(config):

@@ -110,3 +110,27 @@ def test_accepted_path_compaction():
     ek, ev = bf16_bits(kc), bf16_bits(vc)
     R.kv_move(ek, ev, src, dst, cuts)
     assert np.array_equal(bf16_bits(kcd), ek) and np.array_equal(bf16_bits(vcd), ev)
+
+
+def test_tree_split_and_unsplit_paths():
+    """Few sequences: the context is split over CTAs and merged; many: no split."""
+    from nvattn import ops as O
+    parents, _ = tree.build_draft_tree((4, 3, 2, 1, 1, 1), 64)
+    masks = tree.ancestor_masks(parents)
+    for nseq, ctx_hi, expect_split in ((3, 5000, True), (80, 300, False)):
+        rng = np.random.default_rng(nseq)
+        ctx = rng.integers(1, ctx_hi, size=nseq).tolist()
+        n = [64] * nseq
+        g, kc, vc, q, bt = _setup(ctx, n, 32, 8, 40 + nseq)
+        ws = O.tree_workspace_bytes(nseq, 64, sum(n), 32, 8, bt.shape[1], 256)
+        assert (ws > 0) == expect_split
+        all_masks = np.concatenate([masks] * nseq)
+        cq = cu(n)
+        out = ops.tree_attention(q.to(dev), kc.to(dev), vc.to(dev), cq.to(dev),
+                                 torch.tensor(ctx, dtype=torch.int32, device=dev),
+                                 torch.from_numpy(all_masks.view(np.int64)).to(dev), bt.to(dev),
+                                 64, softmax_scale=128 ** -0.5)
+        torch.cuda.synchronize()
+        ref = R.tree_attention(q, kc, vc, cq.numpy(), ctx, all_masks, bt.numpy(), 128 ** -0.5)
+        assert_close(out, ref)
+    assert ops.read_status() == 0

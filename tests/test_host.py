@@ -52,7 +52,7 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     assert rc == _lib.ERR_UNSUPPORTED and b"block_size" in lib.nvattn_last_error()
     rc = lib.nvattn_tree_verify(fake, 256, 128, fake, fake, fake, 256, 128, fake, fake, fake,
                                 fake, 4, 4, 8, 256, 1, 65, 65, 4, 1, 128, ctypes.c_float(0.1),
-                                None, None)
+                                None, 0, None, None)
     assert rc == _lib.ERR_UNSUPPORTED and b"64 tree nodes" in lib.nvattn_last_error()
     rc = lib.nvattn_kv_move(None, None, None, None, None, 2, 4, 256, 100, None, None)
     assert rc == _lib.ERR_INVALID
