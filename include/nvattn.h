@@ -211,7 +211,16 @@ NVATTN_API int nvattn_paged_decode_noalloc(const void* q, int64_t q_stride_tok, 
  *
  *   q, out [total_q][num_heads][head_dim]; caches and block_table as in
  *   nvattn_varlen_prefill's paged mode; tree_mask [total_q] uint64.
+ *
+ * When the sequences alone give too few CTAs, the context is split across
+ * CTAs and merged: the fp32 partials go to `workspace` (device, 256-byte
+ * aligned, >= nvattn_tree_workspace_bytes of the same sizes; 0 bytes means
+ * no split and NULL is accepted). The split depends only on host-side sizes.
  */
+NVATTN_API size_t nvattn_tree_workspace_bytes(int32_t num_seqs, int32_t max_nodes, int64_t total_q,
+                                              int32_t num_heads, int32_t num_kv_heads,
+                                              int32_t max_blocks_per_seq, int32_t block_size);
+
 NVATTN_API int nvattn_tree_verify(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                        const void* k_cache, const void* v_cache,
                        void* out, int64_t o_stride_tok, int64_t o_stride_head,
@@ -221,7 +230,8 @@ NVATTN_API int nvattn_tree_verify(const void* q, int64_t q_stride_tok, int64_t q
                        int32_t max_blocks_per_seq, int32_t num_blocks, int32_t block_size,
                        int32_t num_seqs, int32_t max_nodes, int64_t total_q,
                        int32_t num_heads, int32_t num_kv_heads, int32_t head_dim,
-                       float softmax_scale, int32_t* status, void* stream);
+                       float softmax_scale, void* workspace, size_t workspace_bytes,
+                       int32_t* status, void* stream);
 
 /*
  * In-cache slot moves, grouped (no counterpart in the reference: compaction

@@ -58,7 +58,8 @@ constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int i) { return static_cast<uint32_t>(i) * 128u; }
 __device__ __forceinline__ uint32_t col_o(int i) { return 256u + static_cast<uint32_t>(i) * 128u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
-constexpr int kPolyEvery = 4;  // lean tiles: 1 exp2 pair in 4 from the FMA-pipe polynomial
+constexpr int kPolyEvery = 4;
+constexpr int kPrefetch = 3;   // key tiles of L2 prefetch ahead of the ring  // lean tiles: 1 exp2 pair in 4 from the FMA-pipe polynomial
 
 enum Mode { kDense = 0, kPaged = 1, kTree = 2 };
 
@@ -79,6 +80,13 @@ struct Params {
   int32_t out_vec16;  // output rows 16-byte aligned
   float scale_log2;
   int32_t* status;
+  // Split of the key range over CTAs (tree mode): split s covers key tiles
+  // [s*split_tiles, (s+1)*split_tiles); with nsplit > 1 every CTA writes an
+  // fp32 partial (unnormalised O, reference max, sum) per row to ws_o/ws_ml
+  // and tree_combine_kernel merges them.
+  int32_t nsplit, split_tiles, num_heads;
+  float* ws_o;    // [total_q][num_heads][nsplit][128]
+  float2* ws_ml;  // [total_q][num_heads][nsplit]
 };
 
 struct Barriers {
@@ -111,7 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap vmap, const Params p) {
   const int b = blockIdx.z;
   const int g = blockIdx.y;
-  const int m = gridDim.x - 1 - blockIdx.x;  // heaviest row blocks first
+  const int split = blockIdx.x % p.nsplit;
+  const int m = gridDim.x / p.nsplit - 1 - blockIdx.x / p.nsplit;  // heaviest row blocks first
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -144,7 +153,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     kend = Lk;
   else
     kend = p.causal ? min(Lk, diag + tok_hi + 1) : Lk;
-  const int ntiles = kend > 0 ? (kend + kBN - 1) / kBN : 0;
+  const int ntiles_all = kend > 0 ? (kend + kBN - 1) / kBN : 0;
+  const int jb = split * p.split_tiles;  // first key tile of this CTA's split
+  const int ntiles = max(0, min(ntiles_all, jb + p.split_tiles) - jb);
+  if (p.nsplit > 1 && ntiles == 0) return;  // split past the keys: the merge skips it
 
   if (ntiles == 0) {
     // No visible key for any row of this CTA: the rows are zeros.
@@ -212,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; ok && j < ntiles; ++j) {
         const int st = j % kStages;
         const uint32_t par = ((j / kStages) & 1) ^ 1;
-        const int j0 = j * kBN;
+        const int j0 = (jb + j) * kBN;
         uint8_t* kd = smem + kQBytes + st * 2 * kOperand;
         uint8_t* vd = kd + kOperand;
         int c2 = 0, c3 = 0;  // token coordinate / block coordinate of the tile
@@ -226,6 +238,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           c2 = j0 % p.block_size;
           c3 = blk;
+        }
+        // Warm L2 with the tile kPrefetch ahead: the ring holds one tile of
+        // lookahead, far less than the HBM latency of a cold paged tile.
+        if (j + kPrefetch < ntiles) {
+          const int pj0 = (jb + j + kPrefetch) * kBN;
+          if (MODE == kDense) {
+            const int pc2 = k_begin + pj0;
+            tma_prefetch_3d(&kmap, 0, g, pc2);
+            tma_prefetch_3d(&kmap, 64, g, pc2);
+            tma_prefetch_3d(&vmap, 0, g, pc2);
+            tma_prefetch_3d(&vmap, 64, g, pc2);
+          } else {
+            const int pblk = bt[pj0 / p.block_size];
+            if (pblk >= 0 && pblk < p.num_blocks) {
+              const int pc2 = pj0 % p.block_size;
+              tma_prefetch_4d(&kmap, 0, g, pc2, pblk);
+              tma_prefetch_4d(&kmap, 64, g, pc2, pblk);
+              tma_prefetch_4d(&vmap, 0, g, pc2, pblk);
+              tma_prefetch_4d(&vmap, 64, g, pc2, pblk);
+            }
+          }
         }
         // K ring slot frees after S1 of the tile two back; V after its PV1.
         if (!mbar_wait(&bars->k_empty[st], par)) { ok = false; break; }
@@ -338,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       sm100::fence_after_sync();
-      const int j0 = j * kBN;
+      const int j0 = (jb + j) * kBN;
       const bool full_row = j0 + kBN <= mask_from;  // no key of this tile is masked
       // Raw score or -inf where masked (scale is applied later: it is > 0).
       auto masked = [&](uint32_t raw, int key) -> float {
@@ -478,7 +511,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t orr[32];
       sm100::tmem_ld32(t_lane + col_o(wg) + c * 32, orr);
       sm100::tmem_wait_ld();
-      if (valid && done) {
+      if (valid && done && p.nsplit > 1) {
+        const int64_t slot =
+            (static_cast<int64_t>(q_begin + tok) * p.num_heads + g * group + hh) * p.nsplit + split;
+        float4* dst = reinterpret_cast<float4*>(p.ws_o + slot * kHeadDim + c * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          dst[e] = make_float4(__uint_as_float(orr[4 * e]), __uint_as_float(orr[4 * e + 1]),
+                               __uint_as_float(orr[4 * e + 2]), __uint_as_float(orr[4 * e + 3]));
+        if (c == 0) p.ws_ml[slot] = make_float2(m_used, l);
+      } else if (valid && done) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
@@ -505,6 +547,52 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     sm100::fence_after_sync();
     sm100::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Merges the split-K partials of the tree mode: one warp per (node, query
+// head); lane i owns dims 4i..4i+3. Splits past the sequence's keys were
+// never run and are not read.
+__global__ void __launch_bounds__(128)
+    tree_combine_kernel(const Params p) {
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q_begin = p.cu_q[b];
+  int Lq = p.cu_q[b + 1] - q_begin;
+  if (q_begin < 0 || q_begin > p.total_q) return;
+  if (q_begin + static_cast<int64_t>(Lq) > p.total_q) Lq = static_cast<int>(p.total_q - q_begin);
+  const int idx = blockIdx.x * 4 + warp;
+  const int node = idx / p.num_heads, h = idx % p.num_heads;
+  if (node >= Lq) return;
+  int Lk = p.ctx_lens[b] + Lq;
+  Lk = min(Lk, p.max_blocks * p.block_size);
+  const int ntiles_all = Lk > 0 ? (Lk + kBN - 1) / kBN : 0;
+  const int nact = min(p.nsplit, (ntiles_all + p.split_tiles - 1) / p.split_tiles);
+  const int64_t base = (static_cast<int64_t>(q_begin + node) * p.num_heads + h) * p.nsplit;
+  float mmax = -INFINITY;
+  for (int s = 0; s < nact; ++s) mmax = fmaxf(mmax, p.ws_ml[base + s].x);
+  float L = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < nact; ++s) {
+    const float2 ml = p.ws_ml[base + s];
+    const float w = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - mmax);
+    L += ml.y * w;
+    const float4 o = reinterpret_cast<const float4*>(p.ws_o + (base + s) * kHeadDim)[lane];
+    acc.x += o.x * w;
+    acc.y += o.y * w;
+    acc.z += o.z * w;
+    acc.w += o.w * w;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  __nv_bfloat16* orow = p.out + static_cast<int64_t>(q_begin + node) * p.o_stride_tok +
+                        static_cast<int64_t>(h) * p.o_stride_head + lane * 4;
+  const uint32_t lo = pack_bf16x2(acc.x * inv, acc.y * inv);
+  const uint32_t hi = pack_bf16x2(acc.z * inv, acc.w * inv);
+  if (p.out_vec16) {
+    *reinterpret_cast<uint2*>(orow) = make_uint2(lo, hi);
+  } else {
+    reinterpret_cast<uint32_t*>(orow)[0] = lo;
+    reinterpret_cast<uint32_t*>(orow)[1] = hi;
   }
 }
 
@@ -565,10 +653,16 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, 
   const int blocks_m = (max_tokens + 2 * p.tpt - 1) / (2 * p.tpt);
   if (blocks_m <= 0) return NVATTN_OK;
   if (num_seqs > 65535) return fail(NVATTN_ERR_UNSUPPORTED, "more than 65535 sequences");
-  dim3 grid(blocks_m, p.num_kv_heads, num_seqs);
+  dim3 grid(blocks_m * p.nsplit, p.num_kv_heads, num_seqs);
   attn_tc_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "attn_tc_kernel launch");
+  if (p.nsplit > 1) {
+    const int per_seq = max_tokens * p.num_heads;
+    tree_combine_kernel<<<dim3((per_seq + 3) / 4, num_seqs), 128, 0, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "tree_combine_kernel launch");
+  }
   return NVATTN_OK;
 }
 
@@ -608,14 +702,65 @@ static tc::Params tc_params(void* out, int64_t o_stride_tok, int64_t o_stride_he
   p.tpt = tc::kBM / p.group;
   p.rpt = p.tpt * p.group;
   p.out_vec16 = aligned16(out) && (o_stride_tok * 2) % 16 == 0 && (o_stride_head * 2) % 16 == 0;
+  p.nsplit = 1;
+  p.split_tiles = 1 << 30;
+  p.num_heads = num_heads;
   p.scale_log2 = softmax_scale * kLog2e;
   p.status = status;
   return p;
 }
 
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
+}
+
+// Tree mode: split the key range when the (sequence, KV head, row block)
+// CTAs alone cannot fill ~4 waves of the GPU; splits hold >= 8 key tiles.
+// Depends only on host-side sizes (the block-table width bounds the keys).
+static void tree_split(int num_seqs, int num_heads, int num_kv_heads, int max_nodes,
+                       int max_blocks, int block_size, int* nsplit, int* split_tiles) {
+  const int group = num_heads / num_kv_heads;
+  const int tpt = tc::kBM / group;
+  const int blocks_m = (max_nodes + 2 * tpt - 1) / (2 * tpt);
+  const int64_t ctas = static_cast<int64_t>(num_seqs) * num_kv_heads * blocks_m;
+  const int max_tiles = static_cast<int>(
+      (static_cast<int64_t>(max_blocks) * block_size + tc::kBN - 1) / tc::kBN);
+  int ns = 1;
+  const int64_t target = 4LL * sm_count();
+  if (ctas < target) {
+    ns = static_cast<int>((target + ctas - 1) / ctas);
+    ns = std::min(ns, std::max(1, max_tiles / 8));
+  }
+  *nsplit = std::max(1, ns);
+  *split_tiles = (max_tiles + *nsplit - 1) / *nsplit;
+}
+
+static size_t tree_ws_bytes(int64_t total_q, int num_heads, int nsplit) {
+  if (nsplit <= 1) return 0;
+  const size_t n = static_cast<size_t>(total_q) * num_heads * nsplit;
+  const size_t o_bytes = (n * kHeadDim * sizeof(float) + 255) & ~static_cast<size_t>(255);
+  return o_bytes + n * sizeof(float2);
+}
+
 }  // namespace nvattn
 
 using namespace nvattn;
+
+extern "C" size_t nvattn_tree_workspace_bytes(int32_t num_seqs, int32_t max_nodes, int64_t total_q,
+                                              int32_t num_heads, int32_t num_kv_heads,
+                                              int32_t max_blocks_per_seq, int32_t block_size) {
+  if (num_seqs <= 0 || max_nodes <= 0 || total_q <= 0 || num_heads <= 0 || num_kv_heads <= 0 ||
+      num_heads % num_kv_heads || max_blocks_per_seq <= 0 || block_size <= 0)
+    return 0;
+  int nsplit, split_tiles;
+  tree_split(num_seqs, num_heads, num_kv_heads, max_nodes, max_blocks_per_seq, block_size, &nsplit,
+             &split_tiles);
+  return tree_ws_bytes(total_q, num_heads, nsplit);
+}
 
 extern "C" int nvattn_varlen_prefill(
     const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* k,
@@ -684,7 +829,8 @@ extern "C" int nvattn_tree_verify(const void* q, int64_t q_stride_tok, int64_t q
                                   int32_t num_blocks, int32_t block_size, int32_t num_seqs,
                                   int32_t max_nodes, int64_t total_q, int32_t num_heads,
                                   int32_t num_kv_heads, int32_t head_dim, float softmax_scale,
-                                  int32_t* status, void* stream) {
+                                  void* workspace, size_t workspace_bytes, int32_t* status,
+                                  void* stream) {
   clear_error();
   if (num_seqs < 0 || total_q < 0 || max_nodes < 0)
     return fail(NVATTN_ERR_INVALID, "tree_verify: negative size");
@@ -719,6 +865,20 @@ extern "C" int nvattn_tree_verify(const void* q, int64_t q_stride_tok, int64_t q
   p.num_blocks = num_blocks;
   p.block_size = block_size;
   p.causal = 1;
+  tree_split(num_seqs, num_heads, num_kv_heads, max_nodes, max_blocks_per_seq, block_size,
+             &p.nsplit, &p.split_tiles);
+  const size_t need = tree_ws_bytes(total_q, num_heads, p.nsplit);
+  if (need > 0) {
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(NVATTN_ERR_WORKSPACE,
+                  "tree_verify: workspace smaller than nvattn_tree_workspace_bytes()");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+      return fail(NVATTN_ERR_INVALID, "tree_verify: workspace must be 256-byte aligned");
+    const size_t n = static_cast<size_t>(total_q) * num_heads * p.nsplit;
+    const size_t o_bytes = (n * kHeadDim * sizeof(float) + 255) & ~static_cast<size_t>(255);
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) + o_bytes);
+  }
   return tc::launch<tc::kTree>(qm, km, vm, p, num_seqs, max_nodes,
                                reinterpret_cast<cudaStream_t>(stream));
 }
