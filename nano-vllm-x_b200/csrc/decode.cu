@@ -361,15 +361,17 @@ static int device_sm_count() {
   return n;
 }
 
-// Split size (in 64-token tiles): the largest of 32/16/8/4 tiles that still
-// gives >= 16 CTAs per SM when every sequence is at the block-table width.
+// Split size (in 64-token tiles): the largest of 64/32/16/8/4 tiles that
+// still gives >= 16 CTAs per SM when every sequence is at the block-table
+// width (longer splits amortise each CTA's pipeline fill and shrink the
+// partials the combine reads).
 // Depends only on host-side sizes, so a captured graph keeps its grid.
 static void choose_split(int batch, int num_kv_heads, int max_blocks, int block_size,
                          int* nsplit, int* split_tiles) {
   const int sms = device_sm_count();
   const int64_t max_tiles = (static_cast<int64_t>(max_blocks) * block_size + kTile - 1) / kTile;
   const int64_t pairs = static_cast<int64_t>(batch) * num_kv_heads;
-  int st = 32;
+  int st = 64;
   while (st > 4) {
     const int64_t ns = (max_tiles + st - 1) / st;
     if (pairs * ns >= 16LL * sms) break;
