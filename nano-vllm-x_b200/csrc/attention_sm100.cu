@@ -480,8 +480,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (MODE != kDense && wg == 0 && j == ntiles - 1 && kend - j0 < kBN) {
         // Stale cache rows past the end of the sequence: zero their V so that
         // 0 * NaN cannot reach O. Every tile row r is one 128-byte line in
-        // each half.
+        // each half. V_j must have landed first, or its TMA write would
+        // overwrite the zeros (the slot's previous tile is already consumed:
+        // its P V was issued before S0_j, whose completion brought us here).
         const int vlim = kend - j0;
+        __all_sync(0xffffffffu, mbar_wait(&bars->v_full[j % kStages], (j / kStages) & 1));
         if (r >= vlim) {
           uint8_t* vrow = smem + kQBytes + (j % kStages) * 2 * kOperand + kOperand + r * 128;
           const int4 z = make_int4(0, 0, 0, 0);
