@@ -58,8 +58,8 @@ constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int i) { return static_cast<uint32_t>(i) * 128u; }
 __device__ __forceinline__ uint32_t col_o(int i) { return 256u + static_cast<uint32_t>(i) * 128u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
-constexpr int kPolyEvery = 4;
-constexpr int kPrefetch = 3;   // key tiles of L2 prefetch ahead of the ring  // lean tiles: 1 exp2 pair in 4 from the FMA-pipe polynomial
+constexpr int kPolyEvery = 4;  // lean tiles: 1 exp2 pair in 4 from the FMA-pipe polynomial
+constexpr int kPrefetch = 3;   // key tiles of L2 prefetch ahead of the ring
 
 enum Mode { kDense = 0, kPaged = 1, kTree = 2 };
 
@@ -387,8 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // Tiles where no row of the warp is masked take the lean path.
       const bool wfull = __all_sync(0xffffffffu, full_row);
-      // Pass 1: row max of the raw scores, 64 columns per TMEM round trip.
-      float mraw = -INFINITY;
+      // Pass 1: row max of the raw scores, 64 columns per TMEM round trip,
+      // in four independent chains (a single chain is 64 dependent maxes).
+      float mr4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t sr[64];
@@ -398,14 +399,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (wfull) {
 #pragma unroll
           for (int e = 0; e < 64; e += 2)
-            mraw = fmax3(mraw, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
+            mr4[(e >> 1) & 3] =
+                fmax3(mr4[(e >> 1) & 3], __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]));
         } else {
 #pragma unroll
           for (int e = 0; e < 64; e += 2)
-            mraw = fmax3(mraw, masked(sr[e], j0 + h * 64 + e),
-                         masked(sr[e + 1], j0 + h * 64 + e + 1));
+            mr4[(e >> 1) & 3] = fmax3(mr4[(e >> 1) & 3], masked(sr[e], j0 + h * 64 + e),
+                                      masked(sr[e + 1], j0 + h * 64 + e + 1));
         }
       }
+      const float mraw = fmaxf(fmaxf(mr4[0], mr4[1]), fmaxf(mr4[2], mr4[3]));
       const float mx = (mraw == -INFINITY) ? -INFINITY : mraw * p.scale_log2;
       // Lazy rescale: keep the reference max unless the row max grew by > 2^8.
       float alpha = 1.f;
@@ -425,7 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // of a sub-partition share.
       const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
       const uint64_t nbase2 = pack_f32x2(-base, -base);
-      uint64_t sum2 = pack_f32x2(0.f, 0.f);
+      uint64_t sum2[4] = {pack_f32x2(0.f, 0.f), pack_f32x2(0.f, 0.f), pack_f32x2(0.f, 0.f),
+                          pack_f32x2(0.f, 0.f)};  // four independent sum chains
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t sr[64];
@@ -440,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                           scale2, nbase2);
             const uint64_t p2 = (e % kPolyEvery == kPolyEvery - 1) ? exp2_poly_f32x2(x2)
                                                                     : exp2_mufu_f32x2(x2);
-            sum2 = add_f32x2(sum2, p2);
+            sum2[e & 3] = add_f32x2(sum2[e & 3], p2);
             const float2 pp = unpack_f32x2(p2);
             pk[e] = pack_bf16x2(pp.x, pp.y);
           }
@@ -452,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 pack_f32x2(masked(sr[2 * e], key), masked(sr[2 * e + 1], key + 1)), scale2,
                 nbase2);
             const uint64_t p2 = exp2_mufu_f32x2(x2);
-            sum2 = add_f32x2(sum2, p2);
+            sum2[e & 3] = add_f32x2(sum2[e & 3], p2);
             const float2 pp = unpack_f32x2(p2);
             pk[e] = pack_bf16x2(pp.x, pp.y);
           }
@@ -460,7 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tmem_st32(t_lane + col_s(wg) + h * 32, pk);
       }
       {
-        const float2 sm = unpack_f32x2(sum2);
+        const float2 sm =
+            unpack_f32x2(add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3])));
         l += sm.x + sm.y;
       }
       // O rescale after P is out of registers (keeps the score row and this
