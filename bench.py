@@ -318,6 +318,7 @@ def run_nvattn(args):
         torch.cuda.empty_cache()
         secondary["prefill_cfg3"] = bench_prefill(dev, rank, world, args, tf_peak)
         secondary["tree_verify_cfg5"] = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
+        secondary["qk_norm_rope_store"] = bench_qknorm(dev, rank, world, args, hbm_peak)
         if rank == 0 and world == 1:
             secondary["flash_attn_decode_cfg4"] = bench_flash_attn_decode(dev, args, H, KVH)
 
@@ -473,6 +474,93 @@ def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
                         "[4,3,2,1,1,1], depth 6), 32Q/8KV, d128"}
 
 
+def bench_qknorm(dev, rank, world, args, hbm_peak):
+    """q/k RMSNorm + rotary + KV scatter (qwen3.py:82-86) for one prefill chunk of
+    the e2e model (Qwen3-0.6B: 16Q/8KV heads, 16384 tokens = max_num_batched_tokens),
+    fused into one launch; beside it the reference's own four-launch sequence
+    (compiled RMSNorm x2, compiled rotary, Triton store_kvcache) when the
+    reference package is importable."""
+    from nvattn import ops
+    from nvattn.parallel import head_shard
+    (q0, q1), (k0, k1) = head_shard(16, 8, rank, world)
+    H, KVH, N, max_pos = q1 - q0, k1 - k0, 16384, 40960
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    qkv = torch.randn(N, (H + 2 * KVH) * D, generator=g, device=dev).to(torch.bfloat16)
+    q, k, v = qkv.split([H * D, KVH * D, KVH * D], dim=-1)
+    q, k, v = q.view(N, H, D), k.view(N, KVH, D), v.view(N, KVH, D)
+    pos = torch.randint(0, 4096, (N,), generator=g, device=dev)
+    nb = N // BS + 4
+    slots = torch.randperm(nb * BS, generator=g, device=dev)[:N].to(torch.int32)
+    kc = torch.zeros(nb, BS, KVH, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    w = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, D, 2, dtype=torch.float) / D))
+    freqs = torch.einsum("i,j -> ij", torch.arange(max_pos, dtype=torch.float), inv_freq)
+    cos_sin = torch.cat((freqs.cos(), freqs.sin()), dim=-1).unsqueeze_(1).to(dev)
+    q_out = torch.empty(N, H, D, dtype=torch.bfloat16, device=dev)
+    k_out = torch.empty(N, KVH, D, dtype=torch.bfloat16, device=dev)
+    # algorithmic bytes: q/k/v rows read, q/k written, K/V cache rows written,
+    # plus positions, slots and each token's cos/sin row
+    nbytes = float(N * (H + 2 * KVH) * D * 2 + N * (H + KVH) * D * 2 + 2 * N * KVH * D * 2
+                   + N * (8 + 4 + D * 4))
+
+    def fn():
+        ops.qk_norm_rope_store(pos, q, k, v, w, w, cos_sin, 1e-6, kc, vc, slots,
+                               q_out=q_out, k_out=k_out)
+
+    for _ in range(args.warmup):
+        fn()
+    barrier(world)
+    ms = max_over_ranks(timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps,
+                        world)
+    gbs = sum_over_ranks(nbytes, world) / (ms * 1e-3) / 1e9
+    res = {"metric": "fused q/k-norm+rotary+KV-scatter GB/s", "value": round(gbs, 1),
+           "unit": "GB/s", "ms_per_step": round(ms, 4),
+           "frac_of_measured_hbm_per_gpu": round(gbs / world / hbm_peak, 4),
+           "bytes_per_step": sum_over_ranks(nbytes, world),
+           "workload": "Qwen3-0.6B prefill chunk: 16384 tokens, 16Q/8KV, d128, random slots"}
+    if world == 1:
+        res["reference_four_launch"] = _reference_qknorm(dev, args, pos, q, k, v, w, cos_sin, kc,
+                                                         vc, slots, nbytes)
+    return res
+
+
+def _reference_qknorm(dev, args, pos, q, k, v, w, cos_sin, kc, vc, slots, nbytes):
+    """The reference's modules on the same inputs: RMSNorm (layernorm.py:16-26,
+    torch.compile), RotaryEmbedding (rotary_embedding.py:37-48, torch.compile)
+    and the Triton store_kvcache (attention.py:10-40)."""
+    ref_dir = REPO / "baseline" / "_ref"  # the reference package, when installed there
+    if ref_dir.is_dir() and str(ref_dir) not in sys.path:
+        sys.path.append(str(ref_dir))
+    try:
+        from nanovllm.layers.attention import store_kvcache
+        from nanovllm.layers.layernorm import RMSNorm
+        from nanovllm.layers.rotary_embedding import RotaryEmbedding
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference package not importable: {e!r}"[:200]}
+    try:
+        qn, kn = RMSNorm(D, 1e-6).to(dev), RMSNorm(D, 1e-6).to(dev)
+        with torch.no_grad():
+            qn.weight.copy_(w.float())
+            kn.weight.copy_(w.float())
+        qn, kn = qn.to(torch.bfloat16), kn.to(torch.bfloat16)
+        rope = RotaryEmbedding(D, D, cos_sin.shape[0], 1e6).to(dev)
+
+        def fn():
+            with torch.no_grad():
+                qq, kk = rope(pos, qn(q), kn(k))
+                store_kvcache(kk, v, kc, vc, slots)
+
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        ms = timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+        return {"impl": "reference modules (compiled RMSNorm x2 + rotary, Triton scatter)",
+                "value": round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                "ms_per_step": round(ms, 4)}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference modules did not run: {e!r}"[:200]}
+
+
 def bench_flash_attn_decode(dev, args, H, KVH):
     """The reference's own GPU decode call (flash-attn, attention.py:72-74) on the
     same workload, for comparison; reports why if it cannot run."""
@@ -586,6 +674,8 @@ def run_only(args):
     hbm_peak, tf_peak, _, _ = load_peaks()
     if args.only == "prefill":
         res = bench_prefill(dev, rank, world, args, tf_peak)
+    elif args.only == "qknorm":
+        res = bench_qknorm(dev, rank, world, args, hbm_peak)
     else:
         res = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
     if rank == 0:
@@ -606,7 +696,7 @@ def main():
                     help="decode batch (configs[3] = 128; smaller values only for ncu captures)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
-    ap.add_argument("--only", choices=("prefill", "tree"), default=None,
+    ap.add_argument("--only", choices=("prefill", "tree", "qknorm"), default=None,
                     help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()

@@ -16,6 +16,12 @@
  *   nvattn_tree_verify   ancestor-masked attention of draft-tree nodes
  *   nvattn_kv_move       compaction of the accepted path's K/V slots
  *
+ * and one entry point that fuses the producer side of the path, the steps of
+ * Qwen3Attention.forward between the QKV projection and attention
+ * (nanovllm/models/qwen3.py:82-86 plus the scatter at attention.py:62-63):
+ *
+ *   q_norm/k_norm + rotary_emb + store_kvcache  -> nvattn_qk_norm_rope_store
+ *
  * Conventions (all entry points):
  *   - Pointers are device pointers unless stated otherwise; no torch types.
  *   - Strides are in ELEMENTS (like torch.Tensor.stride()).
@@ -62,7 +68,8 @@ enum nvattn_error {
 enum nvattn_status_bits {
   NVATTN_STATUS_BAD_SLOT = 1,   /* slot_mapping entry outside [-1, num_slots)  */
   NVATTN_STATUS_BAD_BLOCK = 2,  /* block_table entry outside [0, num_blocks)   */
-  NVATTN_STATUS_TIMEOUT = 4     /* a pipeline wait gave up (bounded spin)      */
+  NVATTN_STATUS_TIMEOUT = 4,    /* a pipeline wait gave up (bounded spin)      */
+  NVATTN_STATUS_BAD_POSITION = 8 /* position outside [0, max_position) (clamped) */
 };
 
 /* Message of the last failed call on this host thread ("" if none). */
@@ -247,6 +254,33 @@ NVATTN_API int nvattn_kv_move(void* k_cache, void* v_cache,
                    const int32_t* src_slots, const int32_t* dst_slots,
                    const int32_t* cu_moves, int32_t num_groups, int32_t num_moves,
                    int64_t D, int64_t num_slots, int32_t* status, void* stream);
+
+/*
+ * Fused per-head RMSNorm of q and k, rotary embedding of both, and the K/V
+ * cache scatter: one launch for the four steps of
+ *   q = q_norm(q); k = k_norm(k)                  (layernorm.py:16-26)
+ *   q, k = rotary_emb(positions, q, k)            (rotary_embedding.py:6-14,37-48)
+ *   store_kvcache(k, v, k_cache, v_cache, slots)  (attention.py:10-40)
+ * q (num_tokens x num_heads x 128), k and v (num_tokens x num_kv_heads x 128)
+ * are bf16 rows with the given token strides (views of the fused QKV
+ * projection); heads are contiguous within a token. q_weight/k_weight are the
+ * bf16 RMSNorm weights (128), `cos_sin` the module's fp32 cache
+ * [max_position][cos(64) | sin(64)], `positions` int64 per token.
+ * Writes q_out (contiguous num_tokens x num_heads x 128) and, when non-NULL,
+ * k_out (contiguous num_tokens x num_kv_heads x 128); when slot_mapping is
+ * non-NULL also rotated K and the V row into the caches at each token's slot
+ * (slot -1 skipped, as attention.py:23). All arithmetic is fp32, each step
+ * rounded (no FMA contraction), in the fixed order documented in
+ * csrc/qk_norm_rope.cu, so results are bit-reproducible. Rows must be 8-byte
+ * aligned and cos_sin 16-byte aligned.
+ */
+NVATTN_API int nvattn_qk_norm_rope_store(
+    const void* q, int64_t q_stride_tok, const void* k, int64_t k_stride_tok,
+    const void* v, int64_t v_stride_tok, const void* q_weight, const void* k_weight,
+    const float* cos_sin, int64_t max_position, const int64_t* positions,
+    const int32_t* slot_mapping, void* q_out, void* k_out, void* k_cache, void* v_cache,
+    int64_t num_slots, int64_t num_tokens, int32_t num_heads, int32_t num_kv_heads,
+    int32_t head_dim, float eps, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

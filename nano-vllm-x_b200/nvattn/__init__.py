@@ -10,16 +10,17 @@ from .attention import Attention
 from .context import Context, get_context, reset_context, set_context
 from . import ops, tree, parallel
 from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, kv_move, paged_decode,
-                  store_kvcache, tree_attention, varlen_prefill)
+                  qk_norm_rope_store, store_kvcache, tree_attention, varlen_prefill)
 
 __all__ = [
     "Attention", "Context", "get_context", "set_context", "reset_context", "ops", "tree",
     "parallel", "store_kvcache", "varlen_prefill", "paged_decode", "tree_attention", "kv_move",
-    "flash_attn_varlen_func", "flash_attn_with_kvcache", "install",
+    "flash_attn_varlen_func", "flash_attn_with_kvcache", "qk_norm_rope_store", "install",
 ]
 
 
-def install() -> None:
-    """Replace Nano-vLLM-X's Attention with nvattn's (see nvattn._engine_hook)."""
+def install(fuse_qk_norm_rope: bool = False) -> None:
+    """Replace Nano-vLLM-X's Attention with nvattn's (see nvattn._engine_hook);
+    with ``fuse_qk_norm_rope`` also fuse Qwen3's q/k norm, rotary and KV scatter."""
     from ._engine_hook import install as _install
-    _install()
+    _install(fuse_qk_norm_rope)

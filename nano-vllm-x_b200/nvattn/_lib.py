@@ -24,6 +24,7 @@ ERR_WORKSPACE = 4
 STATUS_BAD_SLOT = 1
 STATUS_BAD_BLOCK = 2
 STATUS_TIMEOUT = 4
+STATUS_BAD_POSITION = 8
 
 _P = c_void_p
 _I32P = c_void_p
@@ -67,6 +68,12 @@ SIGNATURES: dict[str, tuple] = {
                                    c_float, _P, c_size_t, _I32P, _P]),
     "nvattn_kv_move": (c_int, [_P, _P, _I32P, _I32P, _I32P, c_int32, c_int32, c_int64, c_int64,
                                _I32P, _P]),
+    "nvattn_qk_norm_rope_store": (c_int, [_P, c_int64, _P, c_int64, _P, c_int64,  # q, k, v
+                                          _P, _P, _P, c_int64,   # weights, cos_sin, max_position
+                                          _P, _I32P,             # positions, slot_mapping
+                                          _P, _P, _P, _P,        # q_out, k_out, k/v caches
+                                          c_int64, c_int64, c_int32, c_int32, c_int32,
+                                          c_float, _I32P, _P]),
 }
 
 

@@ -13,7 +13,12 @@ nanovllm/layers/attention.py:43-75 exactly:
 * outputs have the reference's shapes: (N, H, d) for prefill and
   (B, 1, H, d) for decode.
 
-All three steps run libnvattn kernels; there is no other code path.
+``forward_fused`` is the same step with the producer side folded in: it
+takes the raw q/k/v split of the QKV projection plus the RMSNorm weights and
+the rotary cache, and one kernel applies q_norm/k_norm and the rotation and
+scatters K/V (qwen3.py:82-86 and attention.py:62-63) before the attention.
+
+All steps run libnvattn kernels; there is no other code path.
 """
 from __future__ import annotations
 
@@ -42,6 +47,30 @@ class Attention(nn.Module):
         k_cache, v_cache = self.k_cache, self.v_cache
         if k_cache.numel() and v_cache.numel():
             ops.store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
+        return self._attend(context, q, k, v)
+
+    def forward_fused(self, positions: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+                      v: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                      cos_sin_cache: torch.Tensor, eps: float):
+        """q_norm/k_norm + rotary_emb + KV scatter in one kernel, then attention.
+
+        q, k, v are the un-normalised split of the QKV projection
+        (qwen3.py:79-81); the result equals ``forward`` applied to the
+        normalised, rotated q and k (qwen3.py:82-86).
+        """
+        context = self.get_context()
+        k_cache, v_cache = self.k_cache, self.v_cache
+        bound = bool(k_cache.numel() and v_cache.numel())
+        # the rotated K itself is read only by dense prefill; the other paths
+        # read K back from the cache
+        need_k = bool(context.is_prefill and context.block_tables is None)
+        q, k = ops.qk_norm_rope_store(positions, q, k, v, q_weight, k_weight, cos_sin_cache, eps,
+                                      k_cache if bound else None, v_cache if bound else None,
+                                      context.slot_mapping if bound else None, need_k=need_k)
+        return self._attend(context, q, k, v)
+
+    def _attend(self, context, q: torch.Tensor, k, v):
+        k_cache, v_cache = self.k_cache, self.v_cache
         if context.is_prefill:
             if context.block_tables is not None:  # prefix cache
                 k, v = k_cache, v_cache

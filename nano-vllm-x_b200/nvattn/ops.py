@@ -11,6 +11,8 @@ on a machine without the CUDA library these functions raise.
     flash_attn_with_kvcache  flash-attn call at attention.py:72-74
     tree_attention           new: EAGLE-style draft-tree verification
     kv_move                  new: in-cache compaction of accepted slots
+    qk_norm_rope_store       q/k RMSNorm + rotary + scatter, the steps of
+                             Qwen3Attention.forward at qwen3.py:82-86
 
 Every launch is asynchronous on ``torch.cuda.current_stream()``, performs
 no host synchronisation and allocates only through torch's caching
@@ -31,6 +33,7 @@ __all__ = [
     "paged_decode",
     "tree_attention",
     "kv_move",
+    "qk_norm_rope_store",
     "decode_workspace_bytes",
     "tree_workspace_bytes",
     "status_tensor",
@@ -371,3 +374,69 @@ def kv_move(k_cache: torch.Tensor, v_cache: torch.Tensor, src_slots: torch.Tenso
               dst_slots.data_ptr(), cu_moves.data_ptr(), cu_moves.numel() - 1, src_slots.numel(),
               D, num_slots,
               _status_ptr(dev), _stream(dev))
+
+
+# ------------------------------------------------------- fused q/k producer side
+
+def qk_norm_rope_store(positions: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+                       v: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                       cos_sin_cache: torch.Tensor, eps: float,
+                       k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+                       slot_mapping: torch.Tensor | None = None, need_k: bool = True,
+                       q_out: torch.Tensor | None = None, k_out: torch.Tensor | None = None
+                       ) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """One launch for ``q = q_norm(q); k = k_norm(k); q, k = rotary_emb(positions, q, k)``
+    (qwen3.py:82-86) plus, when caches and slot_mapping are given, the K/V
+    scatter of ``store_kvcache`` (attention.py:33-40, slot -1 skipped).
+
+    q: (N, H, 128), k/v: (N, KVH, 128) bf16 views with unit element and head
+    strides (the split of the fused QKV projection); q_weight/k_weight: the
+    RMSNorm weights (128,) bf16; cos_sin_cache: the rotary module's fp32
+    buffer (max_position, 1, 128) = [cos | sin]; positions: (N,) int64.
+    Returns (q_rot (N, H, 128), k_rot (N, KVH, 128) or None if not need_k).
+    """
+    dev = _require_cuda(positions, q, k, v, q_weight, k_weight, cos_sin_cache, k_cache, v_cache,
+                        slot_mapping, q_out, k_out)
+    _check_bf16(q, k, v, q_weight, k_weight, k_cache, v_cache, q_out, k_out)
+    N, H, d = q.shape
+    KVH = k.shape[1]
+    if k.shape != (N, KVH, d) or v.shape != (N, KVH, d):
+        raise ValueError("q, k, v token counts or head sizes differ")
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        if t.stride(-1) != 1 or t.stride(1) != d:
+            raise ValueError(f"{n} must have unit element stride and head stride head_dim")
+    if positions.dtype != torch.int64 or positions.numel() != N or not positions.is_contiguous():
+        raise ValueError("positions must be int64 with one entry per token")
+    if cos_sin_cache.dtype != torch.float32 or not cos_sin_cache.is_contiguous() \
+            or cos_sin_cache.shape[-1] != d:
+        raise ValueError("cos_sin_cache must be a contiguous fp32 (max_position, 1, head_dim) tensor")
+    for n, t in (("q_weight", q_weight), ("k_weight", k_weight)):
+        if t.numel() != d or not t.is_contiguous():
+            raise ValueError(f"{n} must be a contiguous ({d},) tensor")
+    max_position = cos_sin_cache.numel() // d
+    if q_out is None:
+        q_out = torch.empty((N, H, d), dtype=torch.bfloat16, device=dev)
+    if k_out is None and need_k:
+        k_out = torch.empty((N, KVH, d), dtype=torch.bfloat16, device=dev)
+    for n, t, shape in (("q_out", q_out, (N, H, d)), ("k_out", k_out, (N, KVH, d))):
+        if t is not None and (tuple(t.shape) != shape or not t.is_contiguous()):
+            raise ValueError(f"{n} must be contiguous {shape}")
+    store = slot_mapping is not None and k_cache is not None and k_cache.numel() > 0
+    num_slots = 0
+    if store:
+        _check_i32("slot_mapping", slot_mapping)
+        if slot_mapping.numel() != N:
+            raise ValueError("slot_mapping must have one entry per token")
+        if not (k_cache.is_contiguous() and v_cache.is_contiguous()) or k_cache.shape != v_cache.shape:
+            raise ValueError("k_cache/v_cache must be contiguous and of equal shape")
+        if k_cache.shape[-2] * k_cache.shape[-1] != KVH * d:
+            raise ValueError("cache rows do not match num_kv_heads * head_dim")
+        num_slots = k_cache.numel() // (KVH * d)
+    _lib.call("nvattn_qk_norm_rope_store", q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0),
+              v.data_ptr(), v.stride(0), q_weight.data_ptr(), k_weight.data_ptr(),
+              cos_sin_cache.data_ptr(), max_position, positions.data_ptr(),
+              slot_mapping.data_ptr() if store else None, q_out.data_ptr(),
+              k_out.data_ptr() if k_out is not None else None,
+              k_cache.data_ptr() if store else None, v_cache.data_ptr() if store else None,
+              num_slots, N, H, KVH, d, float(eps), _status_ptr(dev), _stream(dev))
+    return q_out, k_out

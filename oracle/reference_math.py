@@ -26,6 +26,12 @@ replaces (nanovllm/layers/attention.py):
   (a node sees the whole committed context plus the tree nodes whose bits
   are set in its mask word).
 * ``kv_move``             — grouped in-cache moves, read-all-then-write.
+* ``qk_norm_rope``        — the producer side of the path, Qwen3Attention's
+  q_norm/k_norm (RMSNorm, nanovllm/layers/layernorm.py:16-26) followed by
+  rotary_emb (nanovllm/layers/rotary_embedding.py:6-14,37-48), in numpy
+  float32 with every operation rounded and the reduction in the fixed order
+  the CUDA kernel uses; ``rope_cache`` rebuilds the rotary module's fp32
+  cos/sin buffer (rotary_embedding.py:25-33).
 
 All attention math is float32 on torch CPU tensors (inputs are bf16); the
 result is float32 so tests can state their tolerance against it.
@@ -228,3 +234,88 @@ def padded_block_tables(tables):
     """model_runner.py:123-127: pad rows with -1 to the longest table."""
     width = max(len(t) for t in tables)
     return np.array([list(t) + [-1] * (width - len(t)) for t in tables], dtype=np.int32)
+
+
+# ------------------------------------------------ q/k RMSNorm + rotary (fused)
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bf16 bit patterns (NaN stays NaN)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    b = x.view(np.uint32)
+    r = ((b + np.uint32(0x7FFF) + ((b >> 16) & np.uint32(1))) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        r[nan] = ((b[nan] >> 16) | np.uint32(0x40)).astype(np.uint16)
+    return r
+
+
+def _round_bf16(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+def rope_cache(head_dim: int, max_position: int, base: float) -> torch.Tensor:
+    """The rotary module's buffer, (max_position, 1, head_dim) fp32 = [cos | sin].
+
+    Same torch CPU operations as RotaryEmbedding.__init__
+    (nanovllm/layers/rotary_embedding.py:25-33).
+    """
+    inv_freq = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.float) / head_dim))
+    t = torch.arange(max_position, dtype=torch.float)
+    freqs = torch.einsum("i,j -> ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1).unsqueeze_(1)
+
+
+def qk_norm_rope(x_bits: np.ndarray, w_bits: np.ndarray, cos_sin_rows: np.ndarray,
+                 eps: float) -> np.ndarray:
+    """RMSNorm over the last dim (128) then rotary embedding, bf16 in and out.
+
+    x_bits: (..., 128) uint16 rows; w_bits: (128,) uint16 weight;
+    cos_sin_rows: (..., 128) float32 [cos(64) | sin(64)] of each row's
+    position (broadcast over heads by the caller). Order of operations:
+      lane sums ((x0^2 + x1^2) + x2^2) + x3^2 over dims 4i..4i+3, then a
+      butterfly over lane distances 16, 8, 4, 2, 1; var = sum / 128;
+      r = 1 / sqrt(var + eps); n = bf16(bf16(x * r) * w)   (layernorm.py:20-24)
+      out[:64] = n1*cos - n2*sin; out[64:] = n2*cos + n1*sin (rotary_embedding.py:11-13)
+    """
+    x = bf16_bits_to_f32(x_bits)
+    shape = x.shape
+    assert shape[-1] == 128
+    x = x.reshape(-1, 128)
+    cs = np.broadcast_to(np.asarray(cos_sin_rows, dtype=np.float32), shape).reshape(-1, 128)
+    f32 = np.float32
+    sq = (x * x).reshape(-1, 32, 4)
+    lanes = ((sq[:, :, 0] + sq[:, :, 1]) + sq[:, :, 2]) + sq[:, :, 3]
+    idx = np.arange(32)
+    for off in (16, 8, 4, 2, 1):
+        lanes = lanes + lanes[:, idx ^ off]
+    total = lanes[:, 0]
+    var = total * f32(1.0 / 128.0)
+    r = f32(1.0) / np.sqrt(var + f32(eps))
+    w = bf16_bits_to_f32(w_bits)
+    n = _round_bf16(_round_bf16(x * r[:, None]) * w[None, :])
+    n1, n2 = n[:, :64], n[:, 64:]
+    cos, sin = cs[:, :64], cs[:, 64:]
+    out = np.concatenate(((n1 * cos) - (n2 * sin), (n2 * cos) + (n1 * sin)), axis=1)
+    return f32_to_bf16_bits(out).reshape(shape)
+
+
+def qk_norm_rope_store(positions: np.ndarray, q_bits: np.ndarray, k_bits: np.ndarray,
+                       v_bits: np.ndarray, qw_bits: np.ndarray, kw_bits: np.ndarray,
+                       cos_sin: np.ndarray, eps: float, k_cache=None, v_cache=None,
+                       slot_mapping=None):
+    """q (N,H,128), k/v (N,KVH,128) as uint16; cos_sin (max_pos, 1, 128) fp32.
+
+    Returns (q_rot, k_rot) bit patterns; with caches and slot_mapping also
+    scatters k_rot and v (store_kvcache semantics, slot -1 skipped).
+    """
+    pos = np.asarray(positions, dtype=np.int64)
+    rows = np.asarray(cos_sin, dtype=np.float32).reshape(-1, 128)[pos][:, None, :]
+    q_rot = qk_norm_rope(q_bits, qw_bits, rows, eps)
+    k_rot = qk_norm_rope(k_bits, kw_bits, rows, eps)
+    if slot_mapping is not None and k_cache is not None:
+        store_kvcache(k_rot, np.ascontiguousarray(v_bits), k_cache, v_cache, slot_mapping)
+    return q_rot, k_rot

@@ -1,9 +1,10 @@
 """nvattn inside the reference's own Qwen3 model (configs[1] architecture).
 
 The model (nanovllm/models/qwen3.py) is built once with random weights and
-run twice on the same token sequences: with the reference's attention
-(Triton scatter + flash-attn) and with nvattn.Attention swapped into every
-layer. Decode steps are teacher-forced with the reference's greedy tokens, so
+run three times on the same token sequences: with the reference's attention
+(Triton scatter + flash-attn), with nvattn.Attention swapped into every
+layer, and with q/k RMSNorm + rotary + scatter also fused into one nvattn
+kernel (``install(fuse_qk_norm_rope=True)``). Decode steps are teacher-forced with the reference's greedy tokens, so
 both runs see identical inputs and differences cannot cascade. Per step the
 logits must agree: cosine similarity > 0.999, and the greedy token must match
 wherever the reference's top-2 margin exceeds the bf16 noise of the logits.
@@ -121,8 +122,24 @@ def test_teacher_forced_logits_match_reference_attention():
         for m in attn_modules:
             m.__class__ = nvattn.Attention
         ours = run(forced)
+        # q/k norm + rotary + KV scatter fused into one kernel (qwen3.py:82-86)
+        nvattn.install(fuse_qk_norm_rope=True)
+        fused = run(forced)
     finally:
+        nvattn.install(fuse_qk_norm_rope=False)
         nvattn.Attention.get_context = saved_ctx
+    # the fused kernel rounds the RMSNorm reduction in its own fixed order, so
+    # fused and unfused runs differ like any two reduction orders (28 layers)
+    for a, b in zip(ours, fused):
+        assert torch.nn.functional.cosine_similarity(a, b, dim=-1).min() > 0.999
+    _check_against_reference(ref, fused, steps, lens)
+    _check_against_reference(ref, ours, steps, lens)
+    assert nvattn.ops.read_status() == 0
+    if own_pg:
+        dist.destroy_process_group()
+
+
+def _check_against_reference(ref, ours, steps, lens):
     checked = 0
     for s, (a, b) in enumerate(zip(ref, ours)):
         cos = torch.nn.functional.cosine_similarity(a, b, dim=-1)
@@ -137,6 +154,3 @@ def test_teacher_forced_logits_match_reference_attention():
     print(f"decisive rows checked: {checked} of {(steps + 1) * len(lens)}; min cosine "
           f"{min(torch.nn.functional.cosine_similarity(a, b, dim=-1).min().item() for a, b in zip(ref, ours)):.6f}")
     assert checked >= (steps + 1) * len(lens) // 4
-    assert nvattn.ops.read_status() == 0
-    if own_pg:
-        dist.destroy_process_group()

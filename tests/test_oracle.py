@@ -140,3 +140,44 @@ def test_kv_move_reads_before_writes():
     R.kv_move(kc, vc, np.array([3, 5, 6]), np.array([2, 3, 4]), np.array([0, 3]))
     assert kc[0, 2, 0, 0] == 12 and kc[0, 3, 0, 0] == 20 and kc[0, 4, 0, 0] == 24
     assert vc[0, 3, 0, 0] == 1020
+
+
+def test_qk_norm_rope_oracle_matches_reference_modules():
+    """The fused q/k RMSNorm + rotary restatement against the reference's own
+    RMSNorm and RotaryEmbedding modules (tests/golden/make_qk_norm_golden.py).
+
+    The oracle fixes the order of the sum of squares (the CUDA kernel's
+    butterfly); torch's CPU reduction uses another order, which may move the
+    variance by one fp32 ulp and, rarely, a bf16 rounding: at most 1 ulp on
+    at most 1 in 10^4 elements. The rotary cos/sin buffer is rebuilt exactly.
+    """
+    g = np.load(GOLDEN / "qk_norm_rope_ref.npz")
+    N, H, KVH, D, max_pos = (int(x) for x in g["meta"])
+    cache = R.rope_cache(D, max_pos, float(g["theta"])).numpy().reshape(-1, D)
+    assert np.array_equal(cache[g["positions"]], g["cos_sin_rows"].reshape(-1, D))
+    qkv = g["qkv"]
+    q = qkv[:, :H * D].reshape(N, H, D)
+    k = qkv[:, H * D:(H + KVH) * D].reshape(N, KVH, D)
+    rows = g["cos_sin_rows"].reshape(N, 1, D)
+    for x, w, ref in ((q, g["q_weight"], g["q_rot"]), (k, g["k_weight"], g["k_rot"])):
+        out = R.qk_norm_rope(x, w, rows, float(g["eps"]))
+        ulp = np.abs(out.astype(np.int32) - ref.astype(np.int32))
+        assert ulp.max() <= 1
+        assert (ulp > 0).mean() <= 1e-4
+
+
+def test_qk_norm_rope_oracle_basic_properties():
+    """Rotation preserves the pair norm; position 0 is the identity rotation."""
+    rng = np.random.default_rng(0)
+    x = R.f32_to_bf16_bits(rng.standard_normal((4, 3, 128)).astype(np.float32))
+    w = R.f32_to_bf16_bits(np.ones(128, np.float32))
+    cs = R.rope_cache(128, 16, 1e6).numpy().reshape(-1, 128)
+    out0 = R.qk_norm_rope(x, w, cs[0][None, None, :], 1e-6)
+    xf = R.bf16_bits_to_f32(x).reshape(-1, 128)
+    rms = np.sqrt((xf.astype(np.float64) ** 2).mean(-1, keepdims=True))
+    np.testing.assert_allclose(R.bf16_bits_to_f32(out0).reshape(-1, 128), xf / rms, rtol=1e-2)
+    out5 = R.bf16_bits_to_f32(R.qk_norm_rope(x, w, cs[5][None, None, :], 1e-6)).reshape(-1, 128)
+    a0 = R.bf16_bits_to_f32(out0).reshape(-1, 128)
+    n0 = a0[:, :64] ** 2 + a0[:, 64:] ** 2
+    n5 = out5[:, :64] ** 2 + out5[:, 64:] ** 2
+    np.testing.assert_allclose(n5, n0, rtol=2e-2, atol=1e-3)
