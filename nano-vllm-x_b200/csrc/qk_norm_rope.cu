@@ -42,7 +42,7 @@ __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
-__global__ void __launch_bounds__(kNormWarps * 32, 4)
+__global__ void __launch_bounds__(kNormWarps * 32, 5)
     qk_norm_rope_store_kernel(const char* __restrict__ q, int64_t q_stride_b,
                               const char* __restrict__ k, int64_t k_stride_b,
                               const char* __restrict__ v, int64_t v_stride_b,
@@ -68,8 +68,8 @@ __global__ void __launch_bounds__(kNormWarps * 32, 4)
   const char* qrow = q + tok * q_stride_b;
   const char* krow = k + tok * k_stride_b;
   const char* vrow = v + tok * v_stride_b;
-  const int64_t slot = slot_mapping ? static_cast<int64_t>(slot_mapping[tok]) : -1;
-  const bool store = slot != -1;
+  // V rows are loaded whether or not the token has a slot, so no load waits
+  // on the slot lookup (only padding tokens, slot -1, read V for nothing).
 #pragma unroll
   for (int i = 0; i < kRowsPerWarp; ++i) {
     const int hi = hi0 + i;
@@ -80,9 +80,12 @@ __global__ void __launch_bounds__(kNormWarps * 32, 4)
       raw[i] = __ldg(reinterpret_cast<const uint2*>(qrow + hi * 256) + lane);
     } else {
       raw[i] = __ldg(reinterpret_cast<const uint2*>(krow + (hi - num_heads) * 256) + lane);
-      if (store) vraw[i] = __ldg(reinterpret_cast<const uint2*>(vrow + (hi - num_heads) * 256) + lane);
+      if (slot_mapping)
+        vraw[i] = __ldg(reinterpret_cast<const uint2*>(vrow + (hi - num_heads) * 256) + lane);
     }
   }
+  const int64_t slot = slot_mapping ? static_cast<int64_t>(slot_mapping[tok]) : -1;
+  const bool store = slot != -1;
   int64_t pos = positions[tok];
   if (pos < 0 || pos >= max_position) {
     if (lane == 0 && hi0 == 0) set_status(status, NVATTN_STATUS_BAD_POSITION);

@@ -20,6 +20,8 @@ The engine is used unchanged except for what this environment lacks:
 * attention: ``--attn nvattn`` swaps nanovllm.layers.attention.Attention for
   nvattn.Attention in every engine process (tensor-parallel workers are
   spawned, so the swap runs in ModelRunner's constructor); ``--attn
+  nvattn-fused`` also fuses Qwen3's q/k RMSNorm, rotary and KV scatter into
+  one kernel (``nvattn.install(fuse_qk_norm_rope=True)``); ``--attn
   reference`` keeps the engine's own flash-attn / Triton path.
 
     python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz]
@@ -114,9 +116,9 @@ def patch_engine(attn: str) -> None:
     model_runner.Sampler = sampler.Sampler
     llm_engine.AutoTokenizer = _TokenizerStub
     llm_engine.ModelRunner = E2EModelRunner
-    if attn == "nvattn":
+    if attn in ("nvattn", "nvattn-fused"):
         import nvattn
-        nvattn.install()
+        nvattn.install(fuse_qk_norm_rope=(attn == "nvattn-fused"))
 
 
 def _runner_base():
@@ -201,7 +203,7 @@ def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--tp", type=int, default=1)
-    ap.add_argument("--attn", choices=("nvattn", "reference"), default="nvattn")
+    ap.add_argument("--attn", choices=("nvattn", "nvattn-fused", "reference"), default="nvattn")
     ap.add_argument("--num-seqs", type=int, default=256)
     ap.add_argument("--max-input-len", type=int, default=1024)
     ap.add_argument("--max-output-len", type=int, default=1024)
