@@ -319,6 +319,8 @@ def run_nvattn(args):
         secondary["prefill_cfg3"] = bench_prefill(dev, rank, world, args, tf_peak)
         secondary["tree_verify_cfg5"] = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
         secondary["qk_norm_rope_store"] = bench_qknorm(dev, rank, world, args, hbm_peak)
+        if world == 1:
+            secondary["sampler"] = bench_sampler(dev, args, hbm_peak)
         if rank == 0 and world == 1:
             secondary["flash_attn_decode_cfg4"] = bench_flash_attn_decode(dev, args, H, KVH)
 
@@ -561,6 +563,57 @@ def _reference_qknorm(dev, args, pos, q, k, v, w, cos_sin, kc, vc, slots, nbytes
         return {"unavailable": f"reference modules did not run: {e!r}"[:200]}
 
 
+def bench_sampler(dev, args, hbm_peak):
+    """One decode step's sampling for the e2e batch: 256 rows of Qwen3 logits
+    (vocab 151936, bf16). nvattn's one-pass kernel, sampled (T = 1) and greedy,
+    beside the reference's Sampler (sampler.py:5-12, torch.compile) and
+    torch.argmax when available."""
+    from nvattn import ops
+    B, V = 256, 151936
+    g = torch.Generator(device=dev).manual_seed(21)
+    logits = (torch.randn(B, V, generator=g, device=dev) * 3).to(torch.bfloat16)
+    t = torch.ones(B, dtype=torch.float32, device=dev)
+    out = torch.empty(B, dtype=torch.int64, device=dev)
+    nbytes = float(B * V * 2)
+    res = {"metric": "sampler logits GB/s", "unit": "GB/s",
+           "workload": "256 rows x 151936 bf16 logits (Qwen3 vocab), T = 1 and greedy"}
+    for name, fn in (("sampled", lambda: ops.sample(logits, t, seed=1, offset=0, out=out)),
+                     ("greedy", lambda: ops.sample(logits, out=out))):
+        for _ in range(args.warmup):
+            fn()
+        ms = timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+        res[name] = {"value": round(nbytes / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4),
+                     "frac_of_measured_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4)}
+    res["value"] = res["sampled"]["value"]
+    ref_dir = REPO / "baseline" / "_ref"
+    if ref_dir.is_dir() and str(ref_dir) not in sys.path:
+        sys.path.append(str(ref_dir))
+    try:
+        from nanovllm.layers.sampler import Sampler
+        sampler = Sampler()
+
+        def ref_fn():
+            sampler(logits, t)
+
+        for _ in range(max(args.warmup, 3)):
+            ref_fn()
+        ms = timed(ref_fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+        res["reference_sampler"] = {"impl": "reference Sampler (torch.compile)",
+                                    "value": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                                    "ms_per_step": round(ms, 4)}
+    except Exception as e:  # noqa: BLE001
+        res["reference_sampler"] = {"unavailable": f"{e!r}"[:200]}
+
+    def argmax_fn():
+        torch.argmax(logits, dim=-1)
+
+    for _ in range(args.warmup):
+        argmax_fn()
+    ms = timed(argmax_fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+    res["torch_argmax"] = {"value": round(nbytes / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4)}
+    return res
+
+
 def bench_flash_attn_decode(dev, args, H, KVH):
     """The reference's own GPU decode call (flash-attn, attention.py:72-74) on the
     same workload, for comparison; reports why if it cannot run."""
@@ -676,6 +729,8 @@ def run_only(args):
         res = bench_prefill(dev, rank, world, args, tf_peak)
     elif args.only == "qknorm":
         res = bench_qknorm(dev, rank, world, args, hbm_peak)
+    elif args.only == "sampler":
+        res = bench_sampler(dev, args, hbm_peak)
     else:
         res = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
     if rank == 0:
@@ -696,7 +751,7 @@ def main():
                     help="decode batch (configs[3] = 128; smaller values only for ncu captures)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
-    ap.add_argument("--only", choices=("prefill", "tree", "qknorm"), default=None,
+    ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler"), default=None,
                     help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()

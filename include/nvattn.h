@@ -22,6 +22,10 @@
  *
  *   q_norm/k_norm + rotary_emb + store_kvcache  -> nvattn_qk_norm_rope_store
  *
+ * and one for the consumer side, the sampler (nanovllm/layers/sampler.py:5-12):
+ *
+ *   Sampler.forward / greedy argmax              -> nvattn_sample
+ *
  * Conventions (all entry points):
  *   - Pointers are device pointers unless stated otherwise; no torch types.
  *   - Strides are in ELEMENTS (like torch.Tensor.stride()).
@@ -281,6 +285,20 @@ NVATTN_API int nvattn_qk_norm_rope_store(
     const int32_t* slot_mapping, void* q_out, void* k_out, void* k_cache, void* v_cache,
     int64_t num_slots, int64_t num_tokens, int32_t num_heads, int32_t num_kv_heads,
     int32_t head_dim, float eps, int32_t* status, void* stream);
+
+/*
+ * One token per row of bf16 logits (num_rows x vocab, row stride in
+ * elements), in one pass: with temperatures[r] > 0 a sample from
+ * softmax(logits[r] / T) drawn as argmax(logits/T + Gumbel noise), the same
+ * law as the reference's exponential race (sampler.py:9-11), the noise from
+ * Philox4x32-10 keyed by `seed` with counter (column/4, row, offset)
+ * (24-bit uniforms, so every noise value is finite);
+ * otherwise (temperatures NULL or T <= 0) greedy argmax, first index on
+ * ties. Writes out_tokens[r] (int64).
+ */
+NVATTN_API int nvattn_sample(const void* logits, int64_t row_stride, int64_t num_rows,
+                             int64_t vocab, const float* temperatures, uint64_t seed,
+                             uint64_t offset, int64_t* out_tokens, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

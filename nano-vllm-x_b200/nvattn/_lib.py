@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+from ctypes import c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libnvattn.so"
@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple] = {
                                           _P, _P, _P, _P,        # q_out, k_out, k/v caches
                                           c_int64, c_int64, c_int32, c_int32, c_int32,
                                           c_float, _I32P, _P]),
+    "nvattn_sample": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_uint64, c_uint64, _P, _P]),
 }
 
 

@@ -21,7 +21,8 @@ The engine is used unchanged except for what this environment lacks:
   nvattn.Attention in every engine process (tensor-parallel workers are
   spawned, so the swap runs in ModelRunner's constructor); ``--attn
   nvattn-fused`` also fuses Qwen3's q/k RMSNorm, rotary and KV scatter into
-  one kernel (``nvattn.install(fuse_qk_norm_rope=True)``); ``--attn
+  one kernel (``nvattn.install(fuse_qk_norm_rope=True)``) and takes the greedy
+  token with nvattn's sampler kernel (``nvattn.ops.sample``); ``--attn
   reference`` keeps the engine's own flash-attn / Triton path.
 
     python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz]
@@ -106,13 +107,18 @@ def _greedy_forward(self, logits, temperatures):
     return logits.float().argmax(dim=-1)
 
 
+def _nvattn_greedy_forward(self, logits, temperatures):
+    from nvattn import ops
+    return ops.sample(logits)  # T <= 0 path: greedy argmax, first index on ties
+
+
 def patch_engine(attn: str) -> None:
     """Apply the substitutions listed in the module docstring (idempotent)."""
     import nanovllm.engine.llm_engine as llm_engine
     import nanovllm.engine.model_runner as model_runner
     import nanovllm.layers.sampler as sampler
 
-    sampler.Sampler.forward = _greedy_forward
+    sampler.Sampler.forward = _nvattn_greedy_forward if attn == "nvattn-fused" else _greedy_forward
     model_runner.Sampler = sampler.Sampler
     llm_engine.AutoTokenizer = _TokenizerStub
     llm_engine.ModelRunner = E2EModelRunner

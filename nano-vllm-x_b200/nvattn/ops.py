@@ -13,6 +13,7 @@ on a machine without the CUDA library these functions raise.
     kv_move                  new: in-cache compaction of accepted slots
     qk_norm_rope_store       q/k RMSNorm + rotary + scatter, the steps of
                              Qwen3Attention.forward at qwen3.py:82-86
+    sample                   Sampler.forward (sampler.py:5-12) / greedy argmax
 
 Every launch is asynchronous on ``torch.cuda.current_stream()``, performs
 no host synchronisation and allocates only through torch's caching
@@ -34,6 +35,7 @@ __all__ = [
     "tree_attention",
     "kv_move",
     "qk_norm_rope_store",
+    "sample",
     "decode_workspace_bytes",
     "tree_workspace_bytes",
     "status_tensor",
@@ -440,3 +442,46 @@ def qk_norm_rope_store(positions: torch.Tensor, q: torch.Tensor, k: torch.Tensor
               k_cache.data_ptr() if store else None, v_cache.data_ptr() if store else None,
               num_slots, N, H, KVH, d, float(eps), _status_ptr(dev), _stream(dev))
     return q_out, k_out
+
+
+# -------------------------------------------------------------------- sampling
+
+_sample_calls = 0
+
+
+def sample(logits: torch.Tensor, temperatures: torch.Tensor | None = None,
+           seed: int | None = None, offset: int | None = None,
+           out: torch.Tensor | None = None) -> torch.Tensor:
+    """One token per row of (B, V) bf16 logits, one kernel.
+
+    temperatures (B,) fp32: rows with T > 0 are sampled from softmax(logits/T)
+    (the law of Sampler.forward, sampler.py:5-12); rows with T <= 0, or all
+    rows when temperatures is None, take the greedy argmax (first index on
+    ties, as torch.argmax). The noise is Philox4x32-10 keyed by ``seed``
+    (default: drawn from torch's CPU generator) at counter ``offset``
+    (default: a per-process call count, so repeated calls differ).
+    Returns (B,) int64.
+    """
+    global _sample_calls
+    dev = _require_cuda(logits, temperatures, out)
+    _check_bf16(logits)
+    if logits.dim() != 2 or logits.stride(-1) != 1:
+        raise ValueError("logits must be a (B, V) tensor with unit column stride")
+    B, V = logits.shape
+    if temperatures is not None:
+        if temperatures.dtype != torch.float32 or temperatures.numel() != B \
+                or not temperatures.is_contiguous():
+            raise ValueError("temperatures must be a contiguous float32 (B,) tensor")
+    if seed is None:
+        seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+    if offset is None:
+        offset = _sample_calls
+    _sample_calls += 1
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=dev)
+    elif out.dtype != torch.int64 or out.numel() != B or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int64 (B,) tensor")
+    _lib.call("nvattn_sample", logits.data_ptr(), logits.stride(0), B, V,
+              temperatures.data_ptr() if temperatures is not None else None,
+              int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), out.data_ptr(), _stream(dev))
+    return out

@@ -32,6 +32,11 @@ replaces (nanovllm/layers/attention.py):
   float32 with every operation rounded and the reduction in the fixed order
   the CUDA kernel uses; ``rope_cache`` rebuilds the rotary module's fp32
   cos/sin buffer (rotary_embedding.py:25-33).
+* ``sample_probs`` / ``greedy_tokens`` — the sampler (nanovllm/layers/
+  sampler.py:5-12): its sampling law softmax(logits / T) (the exponential
+  race picks token i with exactly that probability) and argmax for greedy
+  decoding; ``philox4x32_10`` / ``sample_uniforms`` restate the counter-based
+  generator the CUDA sampler draws its noise from (Salmon et al., SC 2011).
 
 All attention math is float32 on torch CPU tensors (inputs are bf16); the
 result is float32 so tests can state their tolerance against it.
@@ -319,3 +324,52 @@ def qk_norm_rope_store(positions: np.ndarray, q_bits: np.ndarray, k_bits: np.nda
     if slot_mapping is not None and k_cache is not None:
         store_kvcache(k_rot, np.ascontiguousarray(v_bits), k_cache, v_cache, slot_mapping)
     return q_rot, k_rot
+
+
+# ------------------------------------------------------------------- sampling
+
+_PHILOX_M = (np.uint64(0xD2511F53), np.uint64(0xCD9E8D57))
+_PHILOX_W = (0x9E3779B9, 0xBB67AE85)
+
+
+def philox4x32_10(ctr: np.ndarray, key) -> np.ndarray:
+    """Philox4x32 with 10 rounds (Salmon, Moraes, Dror, Shaw, SC 2011).
+
+    ctr: (..., 4) uint32 counters; key: two uint32 words. Returns (..., 4) uint32.
+    """
+    c = [np.asarray(ctr, dtype=np.uint64)[..., i] for i in range(4)]
+    k0, k1 = int(key[0]) & 0xFFFFFFFF, int(key[1]) & 0xFFFFFFFF
+    mask = np.uint64(0xFFFFFFFF)
+    for r in range(10):
+        if r:
+            k0 = (k0 + _PHILOX_W[0]) & 0xFFFFFFFF
+            k1 = (k1 + _PHILOX_W[1]) & 0xFFFFFFFF
+        p0 = _PHILOX_M[0] * c[0]
+        p1 = _PHILOX_M[1] * c[2]
+        hi0, lo0 = p0 >> np.uint64(32), p0 & mask
+        hi1, lo1 = p1 >> np.uint64(32), p1 & mask
+        c = [hi1 ^ c[1] ^ np.uint64(k0), lo1, hi0 ^ c[3] ^ np.uint64(k1), lo0]
+    return np.stack(c, axis=-1).astype(np.uint32)
+
+
+def sample_uniforms(row: int, vocab: int, seed: int, offset: int) -> np.ndarray:
+    """The 32-bit noise words of one row: column i takes word i % 4 of
+    Philox4x32-10 at counter (i // 4, row, offset_lo, offset_hi), key (seed_lo, seed_hi)."""
+    n = (vocab + 3) // 4
+    ctr = np.zeros((n, 4), np.uint64)
+    ctr[:, 0] = np.arange(n)
+    ctr[:, 1] = row
+    ctr[:, 2] = offset & 0xFFFFFFFF
+    ctr[:, 3] = (offset >> 32) & 0xFFFFFFFF
+    words = philox4x32_10(ctr, (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF))
+    return words.reshape(-1)[:vocab]
+
+
+def sample_probs(logits: torch.Tensor, temperature: float) -> torch.Tensor:
+    """The reference sampler's law: logits.float() / T, softmax (sampler.py:9-10)."""
+    return torch.softmax(logits.float() / temperature, dim=-1)
+
+
+def greedy_tokens(logits: torch.Tensor) -> torch.Tensor:
+    """argmax over the last dim, first index on ties (torch.argmax)."""
+    return logits.float().argmax(dim=-1)

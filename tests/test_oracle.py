@@ -181,3 +181,31 @@ def test_qk_norm_rope_oracle_basic_properties():
     n0 = a0[:, :64] ** 2 + a0[:, 64:] ** 2
     n5 = out5[:, :64] ** 2 + out5[:, 64:] ** 2
     np.testing.assert_allclose(n5, n0, rtol=2e-2, atol=1e-3)
+
+
+def test_philox_known_answers():
+    """Philox4x32-10 against the known-answer vectors published with the
+    algorithm (Random123 distribution): counter, key -> output."""
+    kat = [((0, 0, 0, 0), (0, 0), (0x6627e8d5, 0xe169c58d, 0xbc57ac4c, 0x9b00dbd8)),
+           ((0xffffffff,) * 4, (0xffffffff,) * 2, (0x408f276d, 0x41c83b0e, 0xa20bc7c6, 0x6d5451fd)),
+           ((0x243f6a88, 0x85a308d3, 0x13198a2e, 0x03707344), (0xa4093822, 0x299f31d0),
+            (0xd16cfe09, 0x94fdcceb, 0x5001e420, 0x24126ea1))]
+    for ctr, key, want in kat:
+        got = R.philox4x32_10(np.array([ctr], dtype=np.uint32), key)[0]
+        assert tuple(int(x) for x in got) == want
+
+
+def test_sampler_law_is_the_exponential_race():
+    """argmax(p / E), E ~ Exp(1) (sampler.py:11) picks i with probability p_i;
+    the Gumbel form argmax(log p + G) used by the kernel is the same law."""
+    g = torch.Generator().manual_seed(0)
+    logits = torch.tensor([[2.0, 1.0, 0.5, -1.0, 0.0]])
+    p = R.sample_probs(logits, 0.7)[0]
+    n = 200000
+    E = torch.empty(n, 5).exponential_(1, generator=g)
+    race = (p[None, :] / E).argmax(-1)
+    G = -torch.log(-torch.log(torch.rand(n, 5, generator=g).clamp_min(1e-12)))
+    gum = (torch.log(p)[None, :] + G).argmax(-1)
+    for picks in (race, gum):
+        freq = torch.bincount(picks, minlength=5).double() / n
+        assert (freq - p.double()).abs().max() < 5e-3
