@@ -275,8 +275,8 @@ NVATTN_API int nvattn_kv_move(void* k_cache, void* v_cache,
  * non-NULL also rotated K and the V row into the caches at each token's slot
  * (slot -1 skipped, as attention.py:23). All arithmetic is fp32, each step
  * rounded (no FMA contraction), in the fixed order documented in
- * csrc/qk_norm_rope.cu, so results are bit-reproducible. Rows must be 8-byte
- * aligned and cos_sin 16-byte aligned.
+ * csrc/qk_norm_rope.cu, so results are bit-reproducible. Rows, weights,
+ * outputs and cos_sin must be 16-byte aligned.
  */
 NVATTN_API int nvattn_qk_norm_rope_store(
     const void* q, int64_t q_stride_tok, const void* k, int64_t k_stride_tok,

@@ -281,8 +281,9 @@ def qk_norm_rope(x_bits: np.ndarray, w_bits: np.ndarray, cos_sin_rows: np.ndarra
     x_bits: (..., 128) uint16 rows; w_bits: (128,) uint16 weight;
     cos_sin_rows: (..., 128) float32 [cos(64) | sin(64)] of each row's
     position (broadcast over heads by the caller). Order of operations:
-      lane sums ((x0^2 + x1^2) + x2^2) + x3^2 over dims 4i..4i+3, then a
-      butterfly over lane distances 16, 8, 4, 2, 1; var = sum / 128;
+      lane sums (((((((x0^2 + x1^2) + x2^2) + x3^2) + x4^2) + x5^2) + x6^2) + x7^2
+      over dims 8i..8i+7 (16 lanes per row), then a butterfly over lane
+      distances 8, 4, 2, 1; var = sum / 128;
       r = 1 / sqrt(var + eps); n = bf16(bf16(x * r) * w)   (layernorm.py:20-24)
       out[:64] = n1*cos - n2*sin; out[64:] = n2*cos + n1*sin (rotary_embedding.py:11-13)
     """
@@ -292,10 +293,12 @@ def qk_norm_rope(x_bits: np.ndarray, w_bits: np.ndarray, cos_sin_rows: np.ndarra
     x = x.reshape(-1, 128)
     cs = np.broadcast_to(np.asarray(cos_sin_rows, dtype=np.float32), shape).reshape(-1, 128)
     f32 = np.float32
-    sq = (x * x).reshape(-1, 32, 4)
-    lanes = ((sq[:, :, 0] + sq[:, :, 1]) + sq[:, :, 2]) + sq[:, :, 3]
-    idx = np.arange(32)
-    for off in (16, 8, 4, 2, 1):
+    sq = (x * x).reshape(-1, 16, 8)
+    lanes = sq[:, :, 0]
+    for e in range(1, 8):
+        lanes = lanes + sq[:, :, e]
+    idx = np.arange(16)
+    for off in (8, 4, 2, 1):
         lanes = lanes + lanes[:, idx ^ off]
     total = lanes[:, 0]
     var = total * f32(1.0 / 128.0)
