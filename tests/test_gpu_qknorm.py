@@ -107,3 +107,77 @@ def test_edge_cases_flags_and_optional_outputs():
     q0, k0 = ops.qk_norm_rope_store(torch.zeros(0, dtype=torch.int64, device=dev), qe, ke, ve, w, w,
                                     cache, 1e-6, kc, vc, torch.zeros(0, dtype=torch.int32, device=dev))
     assert q0.shape == (0, H, d) and k0.shape == (0, KVH, d)
+
+
+def test_fused_decode_step_in_cuda_graph():
+    """Attention.forward_fused in decode mode captured in a CUDA graph on static
+    buffers (as ModelRunner.capture_cudagraph does, model_runner.py:222-257),
+    replayed with new tokens, positions, slots and lengths; every replay equals
+    the eager fused step, and the rotated K/V land in the cache."""
+    import nvattn
+    from nvattn import context as C
+
+    H, KVH, d, bs, width, B = 16, 8, 128, 256, 4, 8
+    nb = B * width
+    gen = torch.Generator().manual_seed(21)
+    kc = (torch.randn(nb, bs, KVH, d, generator=gen) * 0.5).to(torch.bfloat16).to(dev)
+    vc = (torch.randn(nb, bs, KVH, d, generator=gen) * 0.5).to(torch.bfloat16).to(dev)
+    cache = R.rope_cache(d, 4096, 1e6).to(dev)
+    qw = (1 + 0.1 * torch.randn(d, generator=gen)).to(torch.bfloat16).to(dev)
+    kw = (1 + 0.1 * torch.randn(d, generator=gen)).to(torch.bfloat16).to(dev)
+    attn = nvattn.Attention(H, d, d ** -0.5, KVH)
+    attn.k_cache, attn.v_cache = kc, vc
+    # static graph inputs
+    qkv = torch.zeros(B, (H + 2 * KVH) * d, dtype=torch.bfloat16, device=dev)
+    pos = torch.zeros(B, dtype=torch.int64, device=dev)
+    slots = torch.full((B,), -1, dtype=torch.int32, device=dev)
+    lens = torch.zeros(B, dtype=torch.int32, device=dev)
+    bt = torch.arange(nb, dtype=torch.int32, device=dev).view(B, width)
+
+    def step():
+        q, k, v = _split(qkv, H, KVH)
+        return attn.forward_fused(pos, q, k, v, qw, kw, cache, 1e-6)
+
+    saved = nvattn.Attention.__dict__["get_context"]
+    try:
+        nvattn.Attention.get_context = staticmethod(C.get_context)
+        C.set_context(False, slot_mapping=slots, context_lens=lens, block_tables=bt)
+        ops.status_tensor()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = step()
+        for trial in range(3):
+            rng = np.random.default_rng(50 + trial)
+            n = rng.integers(1, width * bs, size=B)  # context length including the new token
+            qkv.copy_((torch.randn(B, (H + 2 * KVH) * d, generator=gen)).to(torch.bfloat16))
+            pos.copy_(torch.from_numpy(n - 1))
+            slot_np = (np.arange(B) * width * bs + (n - 1)).astype(np.int32)
+            slots.copy_(torch.from_numpy(slot_np))
+            lens.copy_(torch.from_numpy(n.astype(np.int32)))
+            kc_before = kc.clone()
+            graph.replay()
+            torch.cuda.synchronize()
+            got = out.clone()
+            k_graph = kc.clone()
+            # eager fused step on the same inputs and the same starting cache
+            kc.copy_(kc_before)
+            want = step()
+            torch.cuda.synchronize()
+            assert torch.equal(got, want)
+            assert torch.equal(k_graph, kc)
+            # the new token's rotated K is in its slot (oracle, bit-exact)
+            q_np = bf16_bits(qkv[:, :H * d].reshape(B, H, d))
+            k_np = bf16_bits(qkv[:, H * d:(H + KVH) * d].reshape(B, KVH, d))
+            _, ek = R.qk_norm_rope_store(n - 1, q_np, k_np, None, bf16_bits(qw), bf16_bits(kw),
+                                         cache.cpu().numpy(), 1e-6)
+            assert np.array_equal(bf16_bits(kc.view(-1, KVH, d)[torch.from_numpy(slot_np).long()]), ek)
+        del graph
+    finally:
+        C.reset_context()
+        nvattn.Attention.get_context = saved
+    assert ops.read_status() == 0
