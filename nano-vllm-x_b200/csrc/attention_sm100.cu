@@ -26,7 +26,9 @@
 //               writes P (bf16 pairs) back over S in TMEM. The output is
 //               rescaled only when the running max grows by more than 2^8
 //               (P then stays <= 256; the final O/l is unchanged), so the
-//               O read-modify-write in TMEM is rare.
+//               O read-modify-write in TMEM is rare. In tree mode a
+//               warpgroup hands P over in two 64-key halves, so the P V of
+//               the first half overlaps the softmax of the second.
 // TMEM columns: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512).
 //
 // Masks (query token i of the sequence, key j):
@@ -97,6 +99,7 @@ struct Barriers {
   uint64_t v_empty[kStages];
   uint64_t s_full[2];
   uint64_t p_full[2];
+  uint64_t p_half[2];  // first 64 keys of P written (tree mode)
   uint64_t o_done;
   uint32_t tmem_base;
 };
@@ -123,6 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m = gridDim.x / p.nsplit - 1 - blockIdx.x / p.nsplit;  // heaviest row blocks first
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Tree mode hands P to the MMA warp in two 64-key halves, so the P V of the
+  // first half overlaps the softmax of the second (measured: +4% on tree,
+  // -2% on prefill, which keeps one hand-off).
+  constexpr bool kSplitP = MODE == kTree;
 
   // ------------------------------------------------ sequence geometry
   const int q_begin = p.cu_q[b];
@@ -191,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_full[i], 4);
+      mbar_init(&bars->p_half[i], 4);
     }
     mbar_init(&bars->o_done, 1);
     fence_barrier_init();
@@ -305,9 +313,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kk > 0 ? 1u : 0u);
         sm100::commit(&bars->s_full[i]);
       };
-      auto issue_pv = [&](int i, int st, int j) {
+      auto issue_pv = [&](int i, int st, int j, int k0, int k1) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int kk = k0; kk < k1; ++kk)
           sm100::mma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, vdesc(v_s(st), kk), idesc_o,
                         (j > 0 || kk > 0) ? 1u : 0u);
       };
@@ -322,20 +330,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % kStages;
         const int nst = (j + 1) % kStages;
         const bool more = j + 1 < ntiles;
-        ok = mbar_wait(&bars->p_full[0], j & 1) && mbar_wait(&bars->v_full[st], (j / kStages) & 1);
-        if (!ok) break;
-        sm100::fence_after_sync();
-        issue_pv(0, st, j);
+        if (kSplitP) {
+          ok = mbar_wait(&bars->p_half[0], j & 1) &&
+               mbar_wait(&bars->v_full[st], (j / kStages) & 1);
+          if (!ok) break;
+          sm100::fence_after_sync();
+          issue_pv(0, st, j, 0, 4);
+          ok = mbar_wait(&bars->p_full[0], j & 1);
+          if (!ok) break;
+          sm100::fence_after_sync();
+          issue_pv(0, st, j, 4, 8);
+        } else {
+          ok = mbar_wait(&bars->p_full[0], j & 1) &&
+               mbar_wait(&bars->v_full[st], (j / kStages) & 1);
+          if (!ok) break;
+          sm100::fence_after_sync();
+          issue_pv(0, st, j, 0, 8);
+        }
         if (more) {
           ok = mbar_wait(&bars->k_full[nst], ((j + 1) / kStages) & 1);
           if (!ok) break;
           sm100::fence_after_sync();
           issue_s(0, nst);
         }
+        if (kSplitP) {
+          ok = mbar_wait(&bars->p_half[1], j & 1);
+          if (!ok) break;
+          sm100::fence_after_sync();
+          issue_pv(1, st, j, 0, 4);
+        }
         ok = mbar_wait(&bars->p_full[1], j & 1);
         if (!ok) break;
         sm100::fence_after_sync();
-        issue_pv(1, st, j);
+        issue_pv(1, st, j, kSplitP ? 4 : 0, 8);
         sm100::commit(&bars->v_empty[st]);
         if (more) {
           issue_s(1, nst);
@@ -419,6 +446,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = mx;
         l *= alpha;
       }
+      if (kSplitP) {
+        // O rescale and stale-V zeroing before any P is handed over: the P V
+        // of the first half may start while the second half is computed.
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          uint32_t orr[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            sm100::tmem_ld32(t_lane + col_o(wg) + c * 32, orr);
+            sm100::tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+            sm100::tmem_st32(t_lane + col_o(wg) + c * 32, orr);
+          }
+        }
+        if (MODE != kDense && wg == 0 && j == ntiles - 1 && kend - j0 < kBN) {
+          // Stale cache rows past the end of the sequence: zero their V so that
+          // 0 * NaN cannot reach O. Every tile row r is one 128-byte line in
+          // each half. V_j must have landed first, or its TMA write would
+          // overwrite the zeros (the slot's previous tile is already consumed:
+          // its P V was issued before S0_j, whose completion brought us here).
+          const int vlim = kend - j0;
+          __all_sync(0xffffffffu, mbar_wait(&bars->v_full[j % kStages], (j / kStages) & 1));
+          if (r >= vlim) {
+            uint8_t* vrow = smem + kQBytes + (j % kStages) * 2 * kOperand + kOperand + r * 128;
+            const int4 z = make_int4(0, 0, 0, 0);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              reinterpret_cast<int4*>(vrow)[c] = z;
+              reinterpret_cast<int4*>(vrow + kHalf)[c] = z;
+            }
+          }
+          fence_proxy_async();
+        }
+      }
       const float base = (m_used == -INFINITY) ? 0.f : m_used;
       // Pass 2: P = exp2(raw*scale - base), two columns per packed fp32x2 FMA,
       // written over S as bf16 pairs. Columns 64h..64h+63 of S become P
@@ -462,6 +524,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         sm100::tmem_st32(t_lane + col_s(wg) + h * 32, pk);
+        if (kSplitP && h == 0) {
+          sm100::tmem_wait_st();
+          sm100::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->p_half[wg]);
+        }
       }
       {
         const float2 sm =
@@ -470,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // O rescale after P is out of registers (keeps the score row and this
       // buffer from being live together).
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
+      if (!kSplitP && j > 0 && __any_sync(0xffffffffu, need)) {
         uint32_t orr[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -482,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           sm100::tmem_st32(t_lane + col_o(wg) + c * 32, orr);
         }
       }
-      if (MODE != kDense && wg == 0 && j == ntiles - 1 && kend - j0 < kBN) {
+      if (!kSplitP && MODE != kDense && wg == 0 && j == ntiles - 1 && kend - j0 < kBN) {
         // Stale cache rows past the end of the sequence: zero their V so that
         // 0 * NaN cannot reach O. Every tile row r is one 128-byte line in
         // each half. V_j must have landed first, or its TMA write would
