@@ -56,6 +56,31 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     assert rc == _lib.ERR_UNSUPPORTED and b"64 tree nodes" in lib.nvattn_last_error()
     rc = lib.nvattn_kv_move(None, None, None, None, None, 2, 4, 256, 100, None, None)
     assert rc == _lib.ERR_INVALID
+    # fused q/k norm + rotary + scatter: head_dim, alignment, NULL pointers, empty batch
+    rc = lib.nvattn_qk_norm_rope_store(fake, 2048, fake, 2048, fake, 2048, fake, fake, fake, 64,
+                                       fake, None, fake, None, None, None, 0, 4, 16, 8, 64,
+                                       ctypes.c_float(1e-6), None, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"head_dim" in lib.nvattn_last_error()
+    rc = lib.nvattn_qk_norm_rope_store(ctypes.c_void_p(0x1008), 4096, fake, 4096, fake, 4096, fake,
+                                       fake, fake, 64, fake, None, fake, None, None, None, 0, 4,
+                                       16, 8, 128, ctypes.c_float(1e-6), None, None)
+    assert rc == _lib.ERR_UNSUPPORTED and b"16-byte" in lib.nvattn_last_error()
+    rc = lib.nvattn_qk_norm_rope_store(fake, 4096, None, 4096, fake, 4096, fake, fake, fake, 64,
+                                       fake, None, fake, None, None, None, 0, 4, 16, 8, 128,
+                                       ctypes.c_float(1e-6), None, None)
+    assert rc == _lib.ERR_INVALID and b"NULL" in lib.nvattn_last_error()
+    rc = lib.nvattn_qk_norm_rope_store(fake, 4096, fake, 4096, fake, 4096, fake, fake, fake, 64,
+                                       fake, fake, fake, None, None, None, 10, 4, 16, 8, 128,
+                                       ctypes.c_float(1e-6), None, None)
+    assert rc == _lib.ERR_INVALID and b"slot_mapping without caches" in lib.nvattn_last_error()
+    assert lib.nvattn_qk_norm_rope_store(None, 4096, None, 4096, None, 4096, None, None, None, 64,
+                                         None, None, None, None, None, None, 0, 0, 16, 8, 128,
+                                         ctypes.c_float(1e-6), None, None) == _lib.OK
+    # sampler: sizes, strides, NULL pointers, empty batch
+    assert lib.nvattn_sample(fake, 100, 4, 0, None, 1, 0, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample(fake, 50, 4, 100, None, 1, 0, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample(None, 100, 4, 100, None, 1, 0, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample(None, 100, 0, 100, None, 1, 0, None, None) == _lib.OK
 
 
 def test_python_wrapper_raises_through_error_path():
@@ -73,6 +98,12 @@ def test_ops_refuse_cpu_tensors_no_fallback():
     with pytest.raises(ValueError, match="CUDA"):
         ops.paged_decode(q, kc, kc, torch.ones(2, dtype=torch.int32),
                          torch.zeros(2, 1, dtype=torch.int32))
+    w = torch.ones(128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.qk_norm_rope_store(torch.zeros(2, dtype=torch.int64), q, k, k, w, w,
+                               torch.zeros(8, 1, 128), 1e-6)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.sample(torch.zeros(2, 10, dtype=torch.bfloat16))
 
 
 def test_store_kvcache_keeps_reference_assertions():
@@ -141,7 +172,8 @@ def test_head_shard_matches_engine_split():
 
 def test_package_surface():
     for name in ("Attention", "store_kvcache", "flash_attn_varlen_func",
-                 "flash_attn_with_kvcache", "tree_attention", "kv_move", "install"):
+                 "flash_attn_with_kvcache", "tree_attention", "kv_move", "qk_norm_rope_store",
+                 "sample", "install"):
         assert hasattr(nvattn, name)
     a = nvattn.Attention(16, 128, 128 ** -0.5, 8)
     assert a.k_cache.numel() == 0 and hasattr(a, "v_cache")
