@@ -321,6 +321,10 @@ def run_nvattn(args):
         secondary["qk_norm_rope_store"] = bench_qknorm(dev, rank, world, args, hbm_peak)
         if world == 1:
             secondary["sampler"] = bench_sampler(dev, args, hbm_peak)
+            try:
+                secondary["layer_cfg0"] = bench_layer_cfg0(dev, args)
+            except Exception as e:  # noqa: BLE001  (a secondary line never sinks the headline)
+                secondary["layer_cfg0"] = {"error": f"{e!r}"[:200]}
         if rank == 0 and world == 1:
             secondary["flash_attn_decode_cfg4"] = bench_flash_attn_decode(dev, args, H, KVH)
 
@@ -468,12 +472,93 @@ def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
                         world)
     tf = sum_over_ranks(flops, world) / (ms * 1e-3) / 1e12
     gbs = sum_over_ranks(nbytes, world) / (ms * 1e-3) / 1e9
+
+    # configs[4] also runs an n-gram linear draft of 8 tokens per sequence:
+    # the same contexts, a chain mask (node i sees nodes 0..i)
+    NL = 8
+    ql = torch.randn(B * NL, H, D, generator=g, device=dev).to(torch.bfloat16)
+    cql = torch.arange(0, (B + 1) * NL, NL, dtype=torch.int32, device=dev)
+    ml = torch.from_numpy(np.tile(tree.chain_masks(NL), B).view(np.int64)).to(dev)
+    outl = torch.empty_like(ql)
+    flops_l = float(sum(4 * D * H * (int(c) + i + 1) for c in ctx for i in range(NL)))
+
+    def fn_l():
+        ops.tree_attention(ql, kc, vc, cql, ctx_d, ml, btd, NL, softmax_scale=D ** -0.5, out=outl)
+
+    for _ in range(args.warmup):
+        fn_l()
+    barrier(world)
+    ms_l = max_over_ranks(timed(fn_l, args.steps, torch.cuda.current_stream(dev)) / args.steps,
+                          world)
+    nbytes_l = float(int(ctx.sum() + B * NL) * KVH * D * 2 * 2)
     return {"metric": "tree-verify attn TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
             "GB_per_s": round(gbs, 1), "ms_per_step": round(ms, 4),
             "frac_of_measured_bf16_peak_per_gpu": round(tf / world / tf_peak, 4),
             "frac_of_measured_hbm_per_gpu": round(gbs / world / hbm_peak, 4),
             "workload": "configs[4]: 32 seqs, ctx U[1024,8192], 64-node tree (branching "
-                        "[4,3,2,1,1,1], depth 6), 32Q/8KV, d128"}
+                        "[4,3,2,1,1,1], depth 6), 32Q/8KV, d128",
+            "linear_draft_8": {
+                "ms_per_step": round(ms_l, 4),
+                "TFLOP_per_s": round(sum_over_ranks(flops_l, world) / (ms_l * 1e-3) / 1e12, 1),
+                "GB_per_s": round(sum_over_ranks(nbytes_l, world) / (ms_l * 1e-3) / 1e9, 1),
+                "frac_of_measured_hbm_per_gpu": round(
+                    sum_over_ranks(nbytes_l, world) / (ms_l * 1e-3) / 1e9 / world / hbm_peak, 4),
+                "workload": "same 32 contexts, 8-token n-gram chain per sequence"}}
+
+
+def bench_layer_cfg0(dev, args):
+    """one attention layer at the Qwen3-0.6B shape (16Q/8KV, d128,
+    block 256) through nvattn.Attention: 4 sequences with prompt lengths
+    U[100,1024] (numpy seed 0), contiguous blocks, one prefill then 32 decode
+    steps. Reports the latency of the whole sequence of calls."""
+    import nvattn
+    from nvattn import context as C
+    H, KVH = 16, 8
+    rng = np.random.default_rng(0)
+    lens = rng.integers(100, 1025, size=4)
+    steps = 32
+    nblk = (lens + steps + BS - 1) // BS
+    starts = np.concatenate([[0], np.cumsum(nblk)[:-1]])
+    nb = int(nblk.sum())
+    g = torch.Generator(device=dev).manual_seed(0)
+    attn = nvattn.Attention(H, D, D ** -0.5, KVH)
+    attn.k_cache = torch.zeros(nb, BS, KVH, D, dtype=torch.bfloat16, device=dev)
+    attn.v_cache = torch.zeros_like(attn.k_cache)
+    saved = nvattn.Attention.__dict__["get_context"]
+    nvattn.Attention.get_context = staticmethod(C.get_context)
+    N = int(lens.sum())
+    q = torch.randn(N, H, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(N, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(N, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    slots_p = torch.tensor(np.concatenate([starts[b] * BS + np.arange(lens[b])
+                                           for b in range(4)]), dtype=torch.int32, device=dev)
+    bt = torch.tensor(np.minimum(np.stack([starts + i for i in range(int(nblk.max()))], axis=1),
+                                 nb - 1), dtype=torch.int32, device=dev)
+    qd = torch.randn(steps, 4, H, D, generator=g, device=dev).to(torch.bfloat16)
+    kd = torch.randn(steps, 4, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    vd = torch.randn(steps, 4, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+    dec = [(torch.tensor(starts * BS + lens + s, dtype=torch.int32, device=dev),
+            torch.tensor(lens + s + 1, dtype=torch.int32, device=dev)) for s in range(steps)]
+
+    def fn():
+        C.set_context(True, cu, cu, int(lens.max()), int(lens.max()), slots_p, None, None)
+        attn(q, k, v)
+        for s in range(steps):
+            C.set_context(False, slot_mapping=dec[s][0], context_lens=dec[s][1], block_tables=bt)
+            attn(qd[s], kd[s], vd[s])
+        C.reset_context()
+
+    try:
+        for _ in range(args.warmup):
+            fn()
+        ms = timed(fn, min(args.steps, 20), torch.cuda.current_stream(dev)) / min(args.steps, 20)
+    finally:
+        nvattn.Attention.get_context = saved
+    return {"metric": "configs[0] layer latency", "value": round(ms, 4), "unit": "ms",
+            "higher_is_better": False,
+            "workload": "configs[0]: 1 attention layer, Qwen3-0.6B shape, 4 seqs U[100,1024], "
+                        "prefill + 32 decode steps (eager, host launch included)"}
 
 
 def bench_qknorm(dev, rank, world, args, hbm_peak):
@@ -731,6 +816,8 @@ def run_only(args):
         res = bench_qknorm(dev, rank, world, args, hbm_peak)
     elif args.only == "sampler":
         res = bench_sampler(dev, args, hbm_peak)
+    elif args.only == "layer":
+        res = bench_layer_cfg0(dev, args)
     else:
         res = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
     if rank == 0:
@@ -751,7 +838,8 @@ def main():
                     help="decode batch (configs[3] = 128; smaller values only for ncu captures)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
-    ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler"), default=None,
+    ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler", "layer"),
+                    default=None,
                     help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")
     args = ap.parse_args()
