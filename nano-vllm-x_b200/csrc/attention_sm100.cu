@@ -37,6 +37,10 @@
 // Keys past the sequence's end in the last tile of the paged cache are stale
 // bytes (maybe NaN): their scores are masked and their V rows zeroed in
 // shared memory before the P V product.
+// Query rows past the sequence (the last row block, short drafts) are never
+// written: a warp with no valid row skips its softmax entirely, and inside a
+// live warp such rows take the unmasked path (rows are independent in both
+// MMAs, so their values cannot reach a valid row).
 #include <algorithm>
 #include <cmath>
 #include <mutex>
@@ -388,6 +392,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (MODE == kTree && valid) mword = p.tree_mask[q_begin + tok];
     // first key index at which this row needs masking
     const int mask_from = !valid ? 0 : (MODE == kTree ? ctx : lim + 1);
+    // A warp whose rows all lie past the sequence (short drafts, the last row
+    // block) computes nothing: its P and O rows are never read. It still
+    // zeroes its share of the stale V rows and hands the tile on.
+    const bool warp_live = __any_sync(0xffffffffu, valid);
 
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -399,7 +407,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       sm100::fence_after_sync();
       const int j0 = (jb + j) * kBN;
-      const bool full_row = j0 + kBN <= mask_from;  // no key of this tile is masked
+      if (!warp_live) {
+        if (MODE != kDense && wg == 0 && j == ntiles - 1 && kend - j0 < kBN) {
+          const int vlim = kend - j0;
+          __all_sync(0xffffffffu, mbar_wait(&bars->v_full[j % kStages], (j / kStages) & 1));
+          if (r >= vlim) {
+            uint8_t* vrow = smem + kQBytes + (j % kStages) * 2 * kOperand + kOperand + r * 128;
+            const int4 z = make_int4(0, 0, 0, 0);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              reinterpret_cast<int4*>(vrow)[c] = z;
+              reinterpret_cast<int4*>(vrow + kHalf)[c] = z;
+            }
+          }
+          fence_proxy_async();
+        }
+        __syncwarp();
+        if (lane == 0) {
+          if (kSplitP) mbar_arrive(&bars->p_half[wg]);
+          mbar_arrive(&bars->p_full[wg]);
+        }
+        continue;
+      }
+      // no key of this tile is masked; rows past the sequence count as
+      // unmasked (their P and O rows are never read)
+      const bool full_row = !valid || j0 + kBN <= mask_from;
       // Raw score or -inf where masked (scale is applied later: it is > 0).
       auto masked = [&](uint32_t raw, int key) -> float {
         const float x = __uint_as_float(raw);
@@ -435,7 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       masked(sr[e + 1], j0 + h * 64 + e + 1));
         }
       }
-      const float mraw = fmaxf(fmaxf(mr4[0], mr4[1]), fmaxf(mr4[2], mr4[3]));
+      // rows past the sequence never move their reference max (no rescales)
+      const float mraw = valid ? fmaxf(fmaxf(mr4[0], mr4[1]), fmaxf(mr4[2], mr4[3])) : -INFINITY;
       const float mx = (mraw == -INFINITY) ? -INFINITY : mraw * p.scale_log2;
       // Lazy rescale: keep the reference max unless the row max grew by > 2^8.
       float alpha = 1.f;
@@ -577,13 +610,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok && lane == 0) set_status(p.status, NVATTN_STATUS_TIMEOUT);
 
     // ----------------------------------------------------------- epilogue
-    const bool done = __all_sync(0xffffffffu, mbar_wait(&bars->o_done, 0));
+    const bool done = !warp_live || __all_sync(0xffffffffu, mbar_wait(&bars->o_done, 0));
     sm100::fence_after_sync();
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
     __nv_bfloat16* orow = p.out + static_cast<int64_t>(q_begin + (valid ? tok : 0)) * p.o_stride_tok +
                           static_cast<int64_t>(g * group + hh) * p.o_stride_head;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 4 && warp_live; ++c) {
       uint32_t orr[32];
       sm100::tmem_ld32(t_lane + col_o(wg) + c * 32, orr);
       sm100::tmem_wait_ld();
