@@ -424,6 +424,7 @@ def bench_prefill(dev, rank, world, args, tf_peak):
     return {"metric": "prefill attn TFLOP/s", "value": round(tfs, 1), "unit": "TFLOP/s",
             "ms_per_step": round(ms, 4),
             "frac_of_measured_bf16_peak_per_gpu": round(tfs / world / tf_peak, 4),
+            "frac_of_measured_bf16_sustained_peak_per_gpu": round(tfs / world / load_peaks()[2], 4),
             "flops_per_step": total,
             "workload": "configs[2]: 64 seqs, 2048-token shared prefix (8 blocks), suffix "
                         "U[128,512], 32Q/8KV, d128, causal over prefix+suffix"}
@@ -494,6 +495,7 @@ def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
     return {"metric": "tree-verify attn TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
             "GB_per_s": round(gbs, 1), "ms_per_step": round(ms, 4),
             "frac_of_measured_bf16_peak_per_gpu": round(tf / world / tf_peak, 4),
+            "frac_of_measured_bf16_sustained_peak_per_gpu": round(tf / world / load_peaks()[2], 4),
             "frac_of_measured_hbm_per_gpu": round(gbs / world / hbm_peak, 4),
             "workload": "configs[4]: 32 seqs, ctx U[1024,8192], 64-node tree (branching "
                         "[4,3,2,1,1,1], depth 6), 32Q/8KV, d128",
