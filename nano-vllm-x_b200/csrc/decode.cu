@@ -362,9 +362,10 @@ static int device_sm_count() {
 }
 
 // Split size (in 64-token tiles): the largest of 64/32/16/8/4 tiles that
-// still gives >= 16 CTAs per SM when every sequence is at the block-table
+// still gives >= 8 CTAs per SM when every sequence is at the block-table
 // width (longer splits amortise each CTA's pipeline fill and shrink the
-// partials the combine reads).
+// partials the combine reads; when one split covers the table, the kernel
+// writes the output itself and no combine runs).
 // Depends only on host-side sizes, so a captured graph keeps its grid.
 static void choose_split(int batch, int num_kv_heads, int max_blocks, int block_size,
                          int* nsplit, int* split_tiles) {
@@ -374,7 +375,7 @@ static void choose_split(int batch, int num_kv_heads, int max_blocks, int block_
   int st = 64;
   while (st > 4) {
     const int64_t ns = (max_tiles + st - 1) / st;
-    if (pairs * ns >= 16LL * sms) break;
+    if (pairs * ns >= 8LL * sms) break;
     st >>= 1;
   }
   *split_tiles = st;
