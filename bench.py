@@ -211,6 +211,26 @@ def timed(fn, steps, stream):
     return start.elapsed_time(end)
 
 
+def graph_timed(fn, steps, dev, per_graph=10):
+    """Device time (ms) of one call of fn: `per_graph` calls captured in one
+    CUDA graph, the graph replayed `steps` times between CUDA events (no
+    host launch gaps between the calls, which a short kernel would show)."""
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(per_graph):
+            fn()
+    graph.replay()
+    stream = torch.cuda.current_stream(dev)
+    ms = timed(graph.replay, steps, stream) / (steps * per_graph)
+    del graph
+    return ms
+
+
 def run_nvattn(args):
     import nvattn
     from nvattn import context as ctxmod
@@ -664,14 +684,34 @@ def bench_sampler(dev, args, hbm_peak):
     nbytes = float(B * V * 2)
     res = {"metric": "sampler logits GB/s", "unit": "GB/s",
            "workload": "256 rows x 151936 bf16 logits (Qwen3 vocab), T = 1 and greedy"}
+    res["timing"] = ("nvattn: 10 calls per CUDA graph, device time per call (3 launches: key "
+                     "reset, chunk kernel, merge); reference and argmax: eager calls")
     for name, fn in (("sampled", lambda: ops.sample(logits, t, seed=1, offset=0, out=out)),
                      ("greedy", lambda: ops.sample(logits, out=out))):
         for _ in range(args.warmup):
             fn()
-        ms = timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+        ms = graph_timed(fn, args.steps, dev)
         res[name] = {"value": round(nbytes / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4),
                      "frac_of_measured_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4)}
+        if args.warmup:
+            ms_eager = timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps
+            res[name]["ms_per_call_eager"] = round(ms_eager, 4)
     res["value"] = res["sampled"]["value"]
+    # one rank's share of vocabulary-parallel sampling at TP2: the pick keys of
+    # its 75,968 columns and the merge of both ranks' keys (the 4 KB all-gather
+    # between them needs a second GPU and is not in this number)
+    half = logits[:, :V // 2]
+    keys2 = torch.zeros(2, B, dtype=torch.int64, device=dev)
+
+    def shard_fn():
+        ops.sample_shard(half, 0, t, seed=1, offset=0, out=keys2[0])
+        ops.sample_merge(keys2, out=out)
+
+    for _ in range(args.warmup):
+        shard_fn()
+    ms = graph_timed(shard_fn, args.steps, dev)
+    res["tp2_rank_shard_sampled"] = {"value": round(nbytes / 2 / (ms * 1e-3) / 1e9, 1),
+                                     "ms_per_step": round(ms, 4)}
     ref_dir = REPO / "baseline" / "_ref"
     if ref_dir.is_dir() and str(ref_dir) not in sys.path:
         sys.path.append(str(ref_dir))

@@ -25,6 +25,8 @@
  * and one for the consumer side, the sampler (nanovllm/layers/sampler.py:5-12):
  *
  *   Sampler.forward / greedy argmax              -> nvattn_sample
+ *   ParallelLMHead gather + sampling at TP > 1   -> nvattn_sample_shard
+ *     (embed_head.py:56-66, sampler.py:5-12)        + nvattn_sample_merge
  *
  * Conventions (all entry points):
  *   - Pointers are device pointers unless stated otherwise; no torch types.
@@ -288,17 +290,43 @@ NVATTN_API int nvattn_qk_norm_rope_store(
 
 /*
  * One token per row of bf16 logits (num_rows x vocab, row stride in
- * elements), in one pass: with temperatures[r] > 0 a sample from
- * softmax(logits[r] / T) drawn as argmax(logits/T + Gumbel noise), the same
- * law as the reference's exponential race (sampler.py:9-11), the noise from
- * Philox4x32-10 keyed by `seed` with counter (column/4, row, offset)
- * (24-bit uniforms, so every noise value is finite);
- * otherwise (temperatures NULL or T <= 0) greedy argmax, first index on
- * ties. Writes out_tokens[r] (int64).
+ * elements): with temperatures[r] > 0 a sample from softmax(logits[r] / T)
+ * drawn as argmax(logits/T + Gumbel noise), the same law as the reference's
+ * exponential race (sampler.py:9-11), the noise from Philox4x32-10 keyed by
+ * `seed` with counter (column/4, row, offset) (24-bit uniforms, so every
+ * noise value is finite); otherwise (temperatures NULL or T <= 0) greedy
+ * argmax, first index on ties. NaN and -inf logits are never picked; a row
+ * with nothing else gives column 0. Writes out_tokens[r] (int64, 8-byte
+ * aligned; it holds intermediate keys until the call's last kernel).
+ * Columns must number below 2^32.
  */
 NVATTN_API int nvattn_sample(const void* logits, int64_t row_stride, int64_t num_rows,
                              int64_t vocab, const float* temperatures, uint64_t seed,
                              uint64_t offset, int64_t* out_tokens, void* stream);
+
+/*
+ * The same pick over one vocabulary shard: logits hold global columns
+ * [vocab_offset, vocab_offset + vocab_shard) of each row (the rank's slice of
+ * ParallelLMHead's output, embed_head.py:56-61), and the noise of column c is
+ * the one nvattn_sample gives column c of the whole row. Writes one 64-bit
+ * key per row (unsigned order = pick order: monotone score bits, then
+ * 0xFFFFFFFF - column; 0 = no candidate). With the same seed, offset and
+ * temperatures on every rank, the largest key over the shards is the key of
+ * nvattn_sample's pick on the gathered row, so ranks exchange num_rows x 8
+ * bytes instead of the logits. vocab_offset % 4 == 0 keeps the vector path.
+ */
+NVATTN_API int nvattn_sample_shard(const void* logits, int64_t row_stride, int64_t num_rows,
+                                   int64_t vocab_shard, int64_t vocab_offset,
+                                   const float* temperatures, uint64_t seed, uint64_t offset,
+                                   uint64_t* out_keys, void* stream);
+
+/*
+ * keys: num_shards x num_rows keys from nvattn_sample_shard (e.g. an
+ * all-gather over the ranks). out_tokens[r] = the column of the largest
+ * keys[s][r] over s, or 0 when no shard has a candidate.
+ */
+NVATTN_API int nvattn_sample_merge(const uint64_t* keys, int64_t num_shards, int64_t num_rows,
+                                   int64_t* out_tokens, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

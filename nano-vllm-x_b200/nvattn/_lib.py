@@ -75,6 +75,9 @@ SIGNATURES: dict[str, tuple] = {
                                           c_int64, c_int64, c_int32, c_int32, c_int32,
                                           c_float, _I32P, _P]),
     "nvattn_sample": (c_int, [_P, c_int64, c_int64, c_int64, _P, c_uint64, c_uint64, _P, _P]),
+    "nvattn_sample_shard": (c_int, [_P, c_int64, c_int64, c_int64, c_int64, _P, c_uint64, c_uint64,
+                                    _P, _P]),
+    "nvattn_sample_merge": (c_int, [_P, c_int64, c_int64, _P, _P]),
 }
 
 

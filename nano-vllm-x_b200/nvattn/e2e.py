@@ -22,8 +22,11 @@ The engine is used unchanged except for what this environment lacks:
   spawned, so the swap runs in ModelRunner's constructor); ``--attn
   nvattn-fused`` also fuses Qwen3's q/k RMSNorm, rotary and KV scatter into
   one kernel (``nvattn.install(fuse_qk_norm_rope=True)``) and takes the greedy
-  token with nvattn's sampler kernel (``nvattn.ops.sample``); ``--attn
-  reference`` keeps the engine's own flash-attn / Triton path.
+  token with nvattn's sampler kernel (``nvattn.ops.sample``); at TP > 1 the
+  LM head no longer gathers its logits to rank 0 (embed_head.py:62-65):
+  every rank picks within its own vocabulary shard and the ranks exchange
+  one 64-bit key per row (``nvattn.parallel.sample_vocab_parallel``);
+  ``--attn reference`` keeps the engine's own flash-attn / Triton path.
 
     python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz]
 
@@ -112,6 +115,17 @@ def _nvattn_greedy_forward(self, logits, temperatures):
     return ops.sample(logits)  # T <= 0 path: greedy argmax, first index on ties
 
 
+def _lm_head_local_forward(self, x):
+    """ParallelLMHead.forward (embed_head.py:53-66) without the gather: each
+    rank returns the logits of its own vocabulary shard."""
+    import torch.nn.functional as F
+    from nanovllm.utils.context import get_context
+    context = get_context()
+    if context.is_prefill:
+        x = x[context.cu_seqlens_q[1:] - 1].contiguous()
+    return F.linear(x, self.weight)
+
+
 def patch_engine(attn: str) -> None:
     """Apply the substitutions listed in the module docstring (idempotent)."""
     import nanovllm.engine.llm_engine as llm_engine
@@ -125,6 +139,9 @@ def patch_engine(attn: str) -> None:
     if attn in ("nvattn", "nvattn-fused"):
         import nvattn
         nvattn.install(fuse_qk_norm_rope=(attn == "nvattn-fused"))
+    if attn == "nvattn-fused":
+        import nanovllm.layers.embed_head as embed_head
+        embed_head.ParallelLMHead.forward = _lm_head_local_forward
 
 
 def _runner_base():
@@ -140,8 +157,29 @@ def _make_runner_class():
         (tensor-parallel workers are started with the spawn method)."""
 
         def __init__(self, config, rank, event):
-            patch_engine(os.environ.get("NVATTN_E2E_ATTN", "nvattn"))
+            self._attn = os.environ.get("NVATTN_E2E_ATTN", "nvattn")
+            self._sample_step = 0
+            patch_engine(self._attn)
             super().__init__(config, rank, event)
+
+        def run(self, seqs, is_prefill):
+            """ModelRunner.run (model_runner.py:214-220); in the fused arm at
+            TP > 1 every rank samples its vocabulary shard and rank 0
+            returns the merged tokens."""
+            if self._attn != "nvattn-fused" or self.world_size == 1:
+                return super().run(seqs, is_prefill)
+            from nanovllm.utils.context import reset_context
+            from nvattn.parallel import sample_vocab_parallel
+            input_ids, positions = (self.prepare_prefill(seqs) if is_prefill
+                                    else self.prepare_decode(seqs))
+            logits = self.run_model(input_ids, positions, is_prefill)
+            tokens = sample_vocab_parallel(logits, None,  # greedy, as the harness decodes
+                                           vocab_offset=self.model.lm_head.vocab_start_idx,
+                                           seed=0, offset=self._sample_step)
+            self._sample_step += 1
+            token_ids = tokens.tolist() if self.rank == 0 else None
+            reset_context()
+            return token_ids
 
     Runner.__module__ = __name__
     Runner.__qualname__ = "E2EModelRunner"

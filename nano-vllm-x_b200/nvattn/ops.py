@@ -485,3 +485,54 @@ def sample(logits: torch.Tensor, temperatures: torch.Tensor | None = None,
               temperatures.data_ptr() if temperatures is not None else None,
               int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), out.data_ptr(), _stream(dev))
     return out
+
+
+def _check_sample_rows(logits: torch.Tensor, temperatures: torch.Tensor | None):
+    _check_bf16(logits)
+    if logits.dim() != 2 or logits.stride(-1) != 1:
+        raise ValueError("logits must be a (B, V) tensor with unit column stride")
+    B = logits.shape[0]
+    if temperatures is not None:
+        if temperatures.dtype != torch.float32 or temperatures.numel() != B \
+                or not temperatures.is_contiguous():
+            raise ValueError("temperatures must be a contiguous float32 (B,) tensor")
+
+
+def sample_shard(logits: torch.Tensor, vocab_offset: int, temperatures: torch.Tensor | None = None,
+                 *, seed: int, offset: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Pick keys of one vocabulary shard: (B, V_shard) bf16 logits holding
+    global columns [vocab_offset, vocab_offset + V_shard).
+
+    Returns (B,) int64 holding each row's 64-bit key (the bits of a uint64;
+    unsigned order = pick order). ``seed`` and ``offset`` are required: every
+    shard of a row must draw the same noise. The largest key over all shards
+    (``sample_merge``) gives the token ``sample`` gives on the whole row.
+    """
+    dev = _require_cuda(logits, temperatures, out)
+    _check_sample_rows(logits, temperatures)
+    B, V = logits.shape
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=dev)
+    elif out.dtype != torch.int64 or out.numel() != B or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int64 (B,) tensor")
+    _lib.call("nvattn_sample_shard", logits.data_ptr(), logits.stride(0), B, V, int(vocab_offset),
+              temperatures.data_ptr() if temperatures is not None else None,
+              int(seed) & (2 ** 64 - 1), int(offset) & (2 ** 64 - 1), out.data_ptr(), _stream(dev))
+    return out
+
+
+def sample_merge(keys: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Tokens from (S, B) int64 keys of S shards (or (B,) for one): the
+    column of each row's largest key, 0 where no shard had a candidate."""
+    dev = _require_cuda(keys, out)
+    if keys.dtype != torch.int64 or not keys.is_contiguous() or keys.dim() not in (1, 2):
+        raise ValueError("keys must be a contiguous int64 (S, B) or (B,) tensor")
+    S, B = (1, keys.shape[0]) if keys.dim() == 1 else keys.shape
+    if out is None:
+        out = torch.empty(B, dtype=torch.int64, device=dev)
+    elif out.dtype != torch.int64 or out.numel() != B or not out.is_contiguous():
+        raise ValueError("out must be a contiguous int64 (B,) tensor")
+    if S == 0:
+        raise ValueError("keys must hold at least one shard")
+    _lib.call("nvattn_sample_merge", keys.data_ptr(), S, B, out.data_ptr(), _stream(dev))
+    return out

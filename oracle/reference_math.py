@@ -376,3 +376,37 @@ def sample_probs(logits: torch.Tensor, temperature: float) -> torch.Tensor:
 def greedy_tokens(logits: torch.Tensor) -> torch.Tensor:
     """argmax over the last dim, first index on ties (torch.argmax)."""
     return logits.float().argmax(dim=-1)
+
+
+def pick_keys(scores: np.ndarray, cols: np.ndarray) -> np.ndarray:
+    """64-bit pick keys of float32 scores at global columns: monotone score
+    bits (-0 folded into +0) in the high word, 0xFFFFFFFF - column in the low
+    word; NaN and -inf give 0 (never picked). Unsigned order = pick order:
+    larger score first, then the lower column."""
+    s = np.asarray(scores, np.float32).copy()
+    s[s == 0] = 0.0
+    b = s.view(np.uint32).astype(np.uint64)
+    neg = (b & np.uint64(0x80000000)) != 0
+    hi = np.where(neg, (~b) & np.uint64(0xFFFFFFFF), b | np.uint64(0x80000000))
+    key = (hi << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.asarray(cols, np.uint64))
+    return np.where(s > -np.inf, key, np.uint64(0))
+
+
+def greedy_shard_keys(logits: torch.Tensor, vocab_offset: int) -> np.ndarray:
+    """Greedy pick key per row of one vocabulary shard of the LM head's
+    logits (embed_head.py:56-61 gives rank r the columns
+    [vocab_offset, vocab_offset + V/tp)): the key of its first maximal column."""
+    x = logits.float().numpy()
+    B, V = x.shape
+    keys = pick_keys(x, np.broadcast_to(np.arange(V, dtype=np.uint64) + np.uint64(vocab_offset),
+                                        (B, V)))
+    return keys.max(axis=1) if V else np.zeros(B, np.uint64)
+
+
+def merge_pick_keys(keys: np.ndarray) -> np.ndarray:
+    """(S, B) uint64 keys -> (B,) int64 tokens: the column of the largest key
+    per row, 0 where every key is 0. Equals sampling the gathered row
+    (embed_head.py:62-65 followed by sampler.py:5-12)."""
+    k = np.asarray(keys, np.uint64).max(axis=0)
+    col = (np.uint64(0xFFFFFFFF) - (k & np.uint64(0xFFFFFFFF))).astype(np.int64)
+    return np.where(k != 0, col, 0)

@@ -5,7 +5,9 @@ collective inside attention (qwen3.py:29-35, model_runner.py:110). These
 tests run two gloo ranks on the CPU: each rank computes the oracle on its own
 head shard (nvattn.parallel.head_shard), the shards are gathered, and the
 result must equal the unsharded computation; the bench's max-over-ranks /
-sum-over-ranks reductions are checked the same way.
+sum-over-ranks reductions are checked the same way. The vocabulary-parallel
+sampler's exchange (nvattn.parallel.gather_pick_keys) runs on oracle keys of
+each rank's vocabulary shard and must give the gathered row's argmax.
 """
 from __future__ import annotations
 
@@ -49,10 +51,18 @@ def _worker(rank, world, port, q, result_q):
                                 q["cu"], q["cu"], 128 ** -0.5, True)
         pparts = [torch.empty_like(pf) for _ in range(world)]
         dist.all_gather(pparts, pf)
+        # vocabulary-parallel sampling: each rank's pick keys over its own
+        # columns, exchanged with one all-gather of B x 8 bytes, merged
+        from nvattn.parallel import gather_pick_keys, vocab_shard
+        v0, v1 = vocab_shard(q["logits"].shape[1], rank, world)
+        keys = torch.from_numpy(R.greedy_shard_keys(q["logits"][:, v0:v1], v0).view(np.int64))
+        all_keys = gather_pick_keys(keys)
+        toks = R.merge_pick_keys(all_keys.numpy().view(np.uint64))
         mx = bench.max_over_ranks(float(rank + 1), world, device="cpu")
         sm = bench.sum_over_ranks(float(rank + 1), world, device="cpu")
         if rank == 0:
-            result_q.put((torch.cat(parts, dim=1).numpy(), torch.cat(pparts, dim=1).numpy(), mx, sm))
+            result_q.put((torch.cat(parts, dim=1).numpy(), torch.cat(pparts, dim=1).numpy(), mx, sm,
+                          toks, tuple(all_keys.shape)))
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -76,8 +86,11 @@ def test_head_sharded_attention_equals_unsharded_world2():
     pq = torch.randn(47, H, 128, generator=g).bfloat16()
     pk = torch.randn(47, KVH, 128, generator=g).bfloat16()
     pv = torch.randn(47, KVH, 128, generator=g).bfloat16()
+    logits = (torch.randn(5, 1000, generator=g) * 3).round().bfloat16()  # ties across the border
+    logits[0, 500] = logits[0, 499] = 50.0
     from conftest import GOLDEN, PROJECT
     payload = dict(H=H, KVH=KVH, q=q, kc=kc, vc=vc, lens=lens, bt=bt, pq=pq, pk=pk, pv=pv, cu=cu,
+                   logits=logits,
                    paths=[str(REPO), str(PROJECT), str(GOLDEN)])
     ctx = mp.get_context("spawn")
     result_q = ctx.SimpleQueue()
@@ -85,7 +98,7 @@ def test_head_sharded_attention_equals_unsharded_world2():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, payload, result_q)) for r in range(2)]
     for p in procs:
         p.start()
-    dec, pre, mx, sm = result_q.get()
+    dec, pre, mx, sm, toks, kshape = result_q.get()
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
@@ -96,3 +109,5 @@ def test_head_sharded_attention_equals_unsharded_world2():
     assert torch.allclose(dec, full_dec, atol=1e-6)
     assert torch.allclose(pre, full_pre, atol=1e-6)
     assert mx == 2.0 and sm == 3.0
+    assert kshape == (2, 5)
+    assert np.array_equal(toks, R.greedy_tokens(logits).numpy()) and toks[0] == 499

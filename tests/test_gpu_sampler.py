@@ -100,3 +100,78 @@ def test_law_matches_reference_sampler():
     tot = ours + ref
     chi2 = (((ours - ref) ** 2) / tot.clamp_min(1)).sum().item()
     assert chi2 < 40.0, chi2
+
+
+def _mixed_rows(B, V, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    logits = (torch.randn(B, V, generator=g, device=dev) * 2).to(torch.bfloat16)
+    t = torch.rand(B, generator=g, device=dev) + 0.5
+    t[::3] = 0.0                      # greedy rows
+    if B > 4:
+        logits[1] = float("-inf")     # no candidate: column 0
+        logits[2, ::2] = float("nan")
+        logits[4, V // 2:] = logits[4].max()  # a tie that spans shard borders
+    return logits, t
+
+
+@pytest.mark.parametrize("B,V,cuts", [(256, 151936, [75968]),
+                                      (33, 151936, [18992, 37984, 75968, 113952]),
+                                      (7, 1003, [1, 498, 998]),      # unaligned: scalar path
+                                      (9, 5000, [2504]), (1, 151936, [8, 151928])])
+def test_vocab_shards_merge_to_the_whole_row_pick(B, V, cuts):
+    """Tensor-parallel LM head (embed_head.py:56-66): each shard's keys,
+    merged, give the token the one-pass sampler gives on the gathered row,
+    bit for bit, for sampled and greedy rows alike."""
+    logits, t = _mixed_rows(B, V, B * 31 + V)
+    seed, offset = 0xABCDEF0123, 17
+    whole = ops.sample(logits, t, seed=seed, offset=offset)
+    bounds = [0] + cuts + [V]
+    keys = torch.stack([ops.sample_shard(logits[:, a:b], a, t, seed=seed, offset=offset)
+                        for a, b in zip(bounds[:-1], bounds[1:])])
+    merged = ops.sample_merge(keys)
+    torch.cuda.synchronize()
+    assert torch.equal(merged, whole)
+    # greedy rows: every shard key equals the oracle's key bit for bit
+    gr = (t <= 0).nonzero().flatten().cpu()
+    for s, (a, b) in enumerate(zip(bounds[:-1], bounds[1:])):
+        want = R.greedy_shard_keys(logits[:, a:b].cpu()[gr], a)
+        assert np.array_equal(keys[s].cpu()[gr].numpy().view(np.uint64), want)
+    if B > 4:
+        assert whole[1].item() == 0
+    lf = logits.float()
+    greedy_whole = R.greedy_tokens(torch.where(torch.isnan(lf), float("-inf"), lf).cpu())
+    assert torch.equal(whole.cpu()[gr], greedy_whole[gr])
+
+
+@pytest.mark.parametrize("V,cut", [(1000, 504), (151936, 75968), (4099, 2050)])
+def test_shard_noise_is_indexed_by_global_column(V, cut):
+    B, seed, offset = 4, 0x1234_5678_9abc_def0, 5
+    logits = torch.zeros(B, V, dtype=torch.bfloat16, device=dev)
+    t = torch.ones(B, dtype=torch.float32, device=dev)
+    keys = torch.stack([ops.sample_shard(logits[:, :cut], 0, t, seed=seed, offset=offset),
+                        ops.sample_shard(logits[:, cut:], cut, t, seed=seed, offset=offset)])
+    got = ops.sample_merge(keys).cpu().numpy()
+    for r in range(B):
+        top = R.sample_uniforms(r, V, seed, offset) >> 8
+        assert top[got[r]] == top.max()
+
+
+def test_sample_and_merge_capture_in_a_cuda_graph():
+    B, V = 64, 151936
+    logits, t = _mixed_rows(B, V, 3)
+    out = torch.empty(B, dtype=torch.int64, device=dev)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ops.sample(logits, t, seed=9, offset=1, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.sample(logits, t, seed=9, offset=1, out=out)
+    for trial in range(3):
+        new, _ = _mixed_rows(B, V, 100 + trial)
+        logits.copy_(new)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ops.sample(logits, t, seed=9, offset=1))
+    del graph

@@ -81,6 +81,19 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     assert lib.nvattn_sample(fake, 50, 4, 100, None, 1, 0, fake, None) == _lib.ERR_INVALID
     assert lib.nvattn_sample(None, 100, 4, 100, None, 1, 0, fake, None) == _lib.ERR_INVALID
     assert lib.nvattn_sample(None, 100, 0, 100, None, 1, 0, None, None) == _lib.OK
+    # vocabulary-shard sampler and merge
+    assert lib.nvattn_sample_shard(fake, 100, 4, 100, -4, None, 1, 0, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample_shard(fake, 100, 4, 100, 2 ** 32 - 50, None, 1, 0, fake,
+                                   None) == _lib.ERR_INVALID
+    assert b"columns" in lib.nvattn_last_error()
+    assert lib.nvattn_sample_shard(fake, 50, 4, 100, 0, None, 1, 0, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample_shard(None, 100, 4, 100, 0, None, 1, 0, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample_shard(None, 100, 0, 100, 8, None, 1, 0, None, None) == _lib.OK
+    assert lib.nvattn_sample_merge(fake, 0, 4, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample_merge(None, 2, 4, fake, None) == _lib.ERR_INVALID
+    assert lib.nvattn_sample_merge(fake, 2, 4, fake, None) == _lib.ERR_INVALID
+    assert b"in place" in lib.nvattn_last_error()
+    assert lib.nvattn_sample_merge(None, 2, 0, None, None) == _lib.OK
 
 
 def test_python_wrapper_raises_through_error_path():
@@ -104,6 +117,10 @@ def test_ops_refuse_cpu_tensors_no_fallback():
                                torch.zeros(8, 1, 128), 1e-6)
     with pytest.raises(ValueError, match="CUDA"):
         ops.sample(torch.zeros(2, 10, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.sample_shard(torch.zeros(2, 10, dtype=torch.bfloat16), 0, seed=1, offset=0)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.sample_merge(torch.zeros(2, 4, dtype=torch.int64))
 
 
 def test_store_kvcache_keeps_reference_assertions():
@@ -168,12 +185,16 @@ def test_head_shard_matches_engine_split():
     assert parallel.head_shard(16, 8, 1, 2) == ((8, 16), (4, 8))
     with pytest.raises(ValueError):
         parallel.head_shard(16, 8, 0, 3)
+    assert parallel.vocab_shard(151936, 1, 2) == (75968, 151936)
+    assert parallel.vocab_shard(151936, 7, 8) == (132944, 151936)
+    with pytest.raises(ValueError):
+        parallel.vocab_shard(151937, 0, 2)
 
 
 def test_package_surface():
     for name in ("Attention", "store_kvcache", "flash_attn_varlen_func",
                  "flash_attn_with_kvcache", "tree_attention", "kv_move", "qk_norm_rope_store",
-                 "sample", "install"):
+                 "sample", "sample_shard", "sample_merge", "install"):
         assert hasattr(nvattn, name)
     a = nvattn.Attention(16, 128, 128 ** -0.5, 8)
     assert a.k_cache.numel() == 0 and hasattr(a, "v_cache")

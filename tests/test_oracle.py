@@ -209,3 +209,32 @@ def test_sampler_law_is_the_exponential_race():
     for picks in (race, gum):
         freq = torch.bincount(picks, minlength=5).double() / n
         assert (freq - p.double()).abs().max() < 5e-3
+
+
+def test_vocab_shard_keys_merge_to_the_gathered_argmax():
+    """Pick keys per vocabulary shard (embed_head.py:56-61) merged over the
+    shards give the first-index argmax of the gathered row
+    (embed_head.py:62-65, then argmax), with ties across shard borders, NaN,
+    all -inf rows and -0 / +0."""
+    g = torch.Generator().manual_seed(0)
+    for trial in range(40):
+        B, V = 9, int(torch.randint(1, 400, (1,), generator=g))
+        x = (torch.randn(B, V, generator=g) * 2).round().bfloat16()  # many exact ties
+        x[0] = float("-inf")
+        x[1, ::3] = float("nan")
+        if V > 2:
+            x[2, :] = float("-inf")
+            x[2, V // 2] = -0.0
+            x[2, V - 1] = 0.0
+        cuts = sorted(set([0, V] + torch.randint(0, V + 1, (3,), generator=g).tolist()))
+        keys = np.stack([R.greedy_shard_keys(x[:, a:b], a) for a, b in zip(cuts[:-1], cuts[1:])])
+        got = R.merge_pick_keys(keys)
+        xf = x.float().clone()
+        xf[torch.isnan(xf)] = float("-inf")
+        want = xf.argmax(-1).numpy()
+        want[(xf == float("-inf")).all(-1).numpy()] = 0
+        assert np.array_equal(got, want), trial
+    # key order: score first, then the lower column
+    k = R.pick_keys(np.array([1.0, 1.0, 2.0, -0.0, 0.0, -np.inf, np.nan], np.float32),
+                    np.array([5, 3, 9, 1, 2, 0, 0]))
+    assert k[1] > k[0] and k[2] > k[1] and k[3] > k[4] and k[5] == 0 and k[6] == 0
