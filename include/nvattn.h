@@ -293,9 +293,10 @@ NVATTN_API int nvattn_qk_norm_rope_store(
  * elements): with temperatures[r] > 0 a sample from softmax(logits[r] / T)
  * drawn as argmax(logits/T + Gumbel noise), the same law as the reference's
  * exponential race (sampler.py:9-11), the noise from Philox4x32-10 keyed by
- * `seed` with counter (column/4, row, offset) (24-bit uniforms, so every
- * noise value is finite); otherwise (temperatures NULL or T <= 0) greedy
- * argmax, first index on ties. NaN and -inf logits are never picked; a row
+ * `seed` with counter (column/4, row, offset) (23-bit uniforms, exact in
+ * fp32 and strictly inside (0, 1), so every noise value is finite);
+ * otherwise (temperatures NULL or T <= 0) greedy argmax, first index on
+ * ties. NaN and -inf logits are never picked; a row
  * with nothing else gives column 0. Writes out_tokens[r] (int64, 8-byte
  * aligned; it holds intermediate keys until the call's last kernel).
  * Columns must number below 2^32.

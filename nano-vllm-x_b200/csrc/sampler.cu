@@ -12,7 +12,7 @@
 // U comes from Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random
 // numbers: as easy as 1, 2, 3", SC 2011): counter (column/4, row,
 // offset_lo, offset_hi), key (seed_lo, seed_hi); the four 32-bit outputs
-// serve columns 4c..4c+3, each mapped to (0, 1) as ((x >> 8) + 0.5) * 2^-24.
+// serve columns 4c..4c+3, each mapped to (0, 1) as ((x >> 9) + 0.5) * 2^-23.
 //
 // Work split: one CTA per (row, column chunk), 16-byte loads of 8 logits
 // where the row allows it. Each CTA folds its best (score, column) into the
@@ -55,13 +55,31 @@ __device__ __forceinline__ uint4 philox4x32_10(uint32_t c0, uint32_t c1, uint32_
   return make_uint4(c[0], c[1], c[2], c[3]);
 }
 
-// Gumbel variable from a 32-bit word: a 24-bit uniform (exact in fp32,
-// strictly inside (0, 1), so the noise is finite), then -log(-log u). The
-// inner log uses the accurate logf: near u = 1, -log u is ~1e-7 and an
-// approximate log's absolute error would swamp it.
+// Gumbel variable from a 32-bit word: a 23-bit uniform u = (k + 0.5) * 2^-23,
+// k = x >> 9. k + 0.5 < 2^23 needs 24 significant bits, so u is exact in
+// fp32 and lies in [2^-24, 1 - 2^-24]: -log u > 0 and the noise is finite
+// (with 24 bits, k + 0.5 would round to 2^24 for the largest k, u to 1 and
+// the noise to +inf). Then -log(-log u). The inner log is the accurate logf:
+// near u = 1, -log u is ~6e-8 and an approximate log's absolute error would
+// swamp it.
 __device__ __forceinline__ float gumbel(uint32_t x) {
-  const float u = (static_cast<float>(x >> 8) + 0.5f) * 5.9604644775390625e-08f;  // 2^-24
+  const float u = (static_cast<float>(x >> 9) + 0.5f) * 1.1920928955078125e-07f;  // 2^-23
   return -__logf(-logf(u));
+}
+
+// No gumbel() value exceeds this: the largest u = 1 - 2^-24 gives
+// -log(-log u) = 16.64, and the margin covers the approximate outer log.
+constexpr float kGumbelBound = 17.0f;
+
+// Largest of the 8 bf16 logits of a 16-byte vector (NaN ignored, as by
+// __hmax2: an all-NaN vector gives NaN).
+__device__ __forceinline__ float vec_max8(const int4 raw) {
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+  const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&raw.z);
+  const __nv_bfloat162 d = *reinterpret_cast<const __nv_bfloat162*>(&raw.w);
+  const __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
+  return fmaxf(__low2float(m), __high2float(m));
 }
 
 // A (score, column) pair as one 64-bit key whose unsigned order is the pick
@@ -102,8 +120,11 @@ __global__ void __launch_bounds__(kSampleThreads, 8)
                         int64_t vocab, int64_t chunk, int64_t num_chunks, uint64_t col0,
                         const float* __restrict__ temperatures, uint64_t seed, uint64_t offset,
                         unsigned long long* __restrict__ keys) {
-  const int64_t row = blockIdx.x / num_chunks;
-  const int64_t c_begin = (blockIdx.x % num_chunks) * chunk;
+  // the host keeps num_rows * num_chunks below 2^31: 32-bit division
+  const uint32_t nch = static_cast<uint32_t>(num_chunks);
+  const uint32_t row32 = blockIdx.x / nch;
+  const int64_t row = row32;
+  const int64_t c_begin = static_cast<int64_t>(blockIdx.x - row32 * nch) * chunk;
   const int64_t c_end = min(vocab, c_begin + chunk);
   const __nv_bfloat16* x = logits + row * row_stride;
   const float t = temperatures ? temperatures[row] : 0.f;
@@ -111,7 +132,7 @@ __global__ void __launch_bounds__(kSampleThreads, 8)
   const float inv_t = greedy ? 1.f : 1.f / t;
   const uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
   const uint32_t o0 = static_cast<uint32_t>(offset), o1 = static_cast<uint32_t>(offset >> 32);
-  const uint32_t r32 = static_cast<uint32_t>(row);
+  const uint32_t r32 = row32;
   float best = -INFINITY;
   uint32_t bcol = 0;
 
@@ -136,8 +157,10 @@ __global__ void __launch_bounds__(kSampleThreads, 8)
       }
     };
     if (greedy) {
-      // memory-bound: four 16-byte loads in flight per thread, then their columns in order
-      const uint32_t none[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      // memory-bound: four 16-byte loads in flight per thread. A vector's
+      // columns are scanned only when its largest logit beats the thread's
+      // best; the scan then takes its first column holding that value (the
+      // order-preserving equivalent of scanning every column with a strict >).
       for (int64_t base = c_begin / 8 + threadIdx.x; base < v_end; base += 4 * kSampleThreads) {
         int4 raw[4];
 #pragma unroll
@@ -146,13 +169,33 @@ __global__ void __launch_bounds__(kSampleThreads, 8)
           raw[u] = vi < v_end ? __ldg(xv + vi) : make_int4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (base + u * kSampleThreads < v_end) take8(raw[u], base + u * kSampleThreads, none);
+        for (int u = 0; u < 4; ++u) {
+          const int64_t vi = base + u * kSampleThreads;
+          if (vi >= v_end) break;
+          const float m = vec_max8(raw[u]);
+          if (m > best) {
+            const uint32_t w[4] = {static_cast<uint32_t>(raw[u].x), static_cast<uint32_t>(raw[u].y),
+                                   static_cast<uint32_t>(raw[u].z), static_cast<uint32_t>(raw[u].w)};
+            int first = 7;
+#pragma unroll
+            for (int e = 7; e >= 0; --e) {
+              const uint32_t bits = (e & 1) ? (w[e >> 1] & 0xffff0000u) : (w[e >> 1] << 16);
+              if (__uint_as_float(bits) == m) first = e;
+            }
+            best = m;
+            bcol = static_cast<uint32_t>(col0 + static_cast<uint64_t>(vi) * 8 + first);
+          }
+        }
       }
     } else {
-      // bound by the noise arithmetic: one vector and two Philox counters per step
+      // bound by the noise arithmetic: one vector and two Philox counters per
+      // step. A vector none of whose columns can beat the thread's best
+      // (largest logit / T + the noise bound below it, with the same rounded
+      // fma, hence an upper bound of every score in the vector) skips the
+      // noise: its columns would never be picked.
       for (int64_t vi = c_begin / 8 + threadIdx.x; vi < v_end; vi += kSampleThreads) {
         const int4 raw = __ldg(xv + vi);
+        if (__fmaf_rn(vec_max8(raw), inv_t, kGumbelBound) < best) continue;
         const uint32_t c = static_cast<uint32_t>((col0 + static_cast<uint64_t>(vi) * 8) >> 2);
         const uint4 r0 = philox4x32_10(c, r32, o0, o1, k0, k1);
         const uint4 r1 = philox4x32_10(c + 1, r32, o0, o1, k0, k1);
