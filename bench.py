@@ -345,6 +345,10 @@ def run_nvattn(args):
                 secondary["layer_cfg0"] = bench_layer_cfg0(dev, args)
             except Exception as e:  # noqa: BLE001  (a secondary line never sinks the headline)
                 secondary["layer_cfg0"] = {"error": f"{e!r}"[:200]}
+            try:
+                secondary["decode_prepare"] = bench_decode_prepare(dev, args)
+            except Exception as e:  # noqa: BLE001
+                secondary["decode_prepare"] = {"error": f"{e!r}"[:200]}
         if rank == 0 and world == 1:
             secondary["flash_attn_decode_cfg4"] = bench_flash_attn_decode(dev, args, H, KVH)
 
@@ -750,6 +754,90 @@ def bench_sampler(dev, args, hbm_peak):
     return res
 
 
+def bench_decode_prepare(dev, args):
+    """One decode step's metadata for the e2e batch: 256 sequences of
+    U[100, 2048] tokens in 256-token blocks, written into CUDA-graph inputs of
+    512 rows x 16 blocks. The reference arm runs the reference's own
+    ModelRunner.prepare_decode and run_model (model_runner.py:172-188,
+    196-212) on a stand-in runner whose graph replay and logits are no-ops;
+    nvattn packs one record and launches nvattn_decode_prepare. Host wall
+    time per step with a synchronisation after each step, as the engine
+    synchronises on its sampled tokens."""
+    import random
+    import time
+    from types import SimpleNamespace
+
+    from nvattn.decode_meta import DecodeMetadata
+    ref_dir = REPO / "baseline" / "_ref"
+    if ref_dir.is_dir() and str(ref_dir) not in sys.path:
+        sys.path.append(str(ref_dir))
+    try:
+        from nanovllm.engine.model_runner import ModelRunner
+        from nanovllm.engine.sequence import Sequence
+        from nanovllm.sampling_params import SamplingParams
+        from nanovllm.utils.context import reset_context
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference engine not importable: {e!r}"[:200]}
+    rnd = random.Random(0)
+    seqs = []
+    for i in range(256):
+        s = Sequence([rnd.randint(0, 10000) for _ in range(rnd.randint(100, 2048))],
+                     SamplingParams(ignore_eos=True, max_tokens=64))
+        s.block_table = list(range(i * 16, i * 16 + (len(s) + 255) // 256))
+        seqs.append(s)
+    rows, width = 512, 16
+
+    def graph_vars():
+        return dict(input_ids=torch.zeros(rows, dtype=torch.int64, device=dev),
+                    positions=torch.zeros(rows, dtype=torch.int64, device=dev),
+                    slot_mapping=torch.zeros(rows, dtype=torch.int32, device=dev),
+                    context_lens=torch.zeros(rows, dtype=torch.int32, device=dev),
+                    block_tables=torch.zeros(rows, width, dtype=torch.int32, device=dev),
+                    outputs=torch.zeros(rows, 8, device=dev))
+
+    fake = SimpleNamespace(block_size=256, enforce_eager=False, graph_bs=[256, 512],
+                           graphs={256: SimpleNamespace(replay=lambda: None),
+                                   512: SimpleNamespace(replay=lambda: None)},
+                           graph_vars=graph_vars(),
+                           model=SimpleNamespace(compute_logits=lambda x: None))
+    fake.prepare_block_tables = lambda ss: ModelRunner.prepare_block_tables(fake, ss)
+
+    def ref_step():
+        ids, pos = ModelRunner.prepare_decode(fake, seqs)
+        ModelRunner.run_model(fake, ids, pos, False)
+        reset_context()
+
+    meta = DecodeMetadata(512, width, 256, dev)
+    gv = graph_vars()
+    del gv["outputs"]
+
+    def nv_step():
+        meta.pack(seqs)
+        meta.launch(rows, **gv)
+
+    def wall(fn):
+        for _ in range(args.warmup):
+            fn()
+            torch.cuda.synchronize(dev)
+        n = max(args.steps, 20)
+        t = time.perf_counter()
+        for _ in range(n):
+            fn()
+            torch.cuda.synchronize(dev)
+        return (time.perf_counter() - t) / n * 1e3
+
+    ms_ref = wall(ref_step)
+    ms_nv = wall(nv_step)
+    # the same outputs from both paths
+    same = all(torch.equal(fake.graph_vars[k], gv[k]) for k in gv)
+    return {"metric": "decode-step metadata, host wall ms per step", "unit": "ms",
+            "higher_is_better": False, "value": round(ms_nv, 4),
+            "reference_prepare_decode_and_copies": round(ms_ref, 4),
+            "outputs_identical": bool(same), "gpu_launches_per_step": 1,
+            "workload": "256 sequences, U[100, 2048] tokens, 256-token blocks; graph inputs "
+                        "512 rows x 16 blocks; synchronised each step"}
+
+
 def bench_flash_attn_decode(dev, args, H, KVH):
     """The reference's own GPU decode call (flash-attn, attention.py:72-74) on the
     same workload, for comparison; reports why if it cannot run."""
@@ -869,6 +957,8 @@ def run_only(args):
         res = bench_sampler(dev, args, hbm_peak)
     elif args.only == "layer":
         res = bench_layer_cfg0(dev, args)
+    elif args.only == "prep":
+        res = bench_decode_prepare(dev, args)
     else:
         res = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
     if rank == 0:
@@ -889,7 +979,7 @@ def main():
                     help="decode batch (configs[3] = 128; smaller values only for ncu captures)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
-    ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler", "layer"),
+    ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler", "layer", "prep"),
                     default=None,
                     help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")

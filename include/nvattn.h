@@ -28,6 +28,12 @@
  *   ParallelLMHead gather + sampling at TP > 1   -> nvattn_sample_shard
  *     (embed_head.py:56-66, sampler.py:5-12)        + nvattn_sample_merge
  *
+ * and one for the decode step's metadata (ModelRunner.prepare_decode plus
+ * the copies into the decode graph's inputs, model_runner.py:172-188,
+ * 204-210):
+ *
+ *   prepare_decode + graph_vars copies           -> nvattn_decode_prepare
+ *
  * Conventions (all entry points):
  *   - Pointers are device pointers unless stated otherwise; no torch types.
  *   - Strides are in ELEMENTS (like torch.Tensor.stride()).
@@ -328,6 +334,39 @@ NVATTN_API int nvattn_sample_shard(const void* logits, int64_t row_stride, int64
  */
 NVATTN_API int nvattn_sample_merge(const uint64_t* keys, int64_t num_shards, int64_t num_rows,
                                    int64_t* out_tokens, void* stream);
+
+/*
+ * Decode-step metadata from one packed host record per sequence.
+ * packed layout (num_seqs = B, table_width = W, 8-byte aligned):
+ *   int64 last_token[B] | int32 num_tokens[B] | int32 table_len[B] |
+ *   int32 block_table[B][W]  (each row padded with -1)
+ * num_tokens is len(seq) with the new token (sequence.py:33), table_len is
+ * len(seq.block_table). If packed_host is non-NULL the call first copies the
+ * record (nvattn_decode_prepare_bytes(B, W) bytes) into packed_dev on the
+ * stream (use pinned memory, and keep it unchanged until the copy is done);
+ * with packed_host NULL, packed_dev already holds it. Then one kernel writes,
+ * for r < B:
+ *   input_ids[r] = last_token, positions[r] = num_tokens - 1,
+ *   context_lens[r] = num_tokens,
+ *   slot_mapping[r] = block_table[r][table_len-1] * block_size
+ *       + num_tokens - (ceil(num_tokens / block_size) - 1) * block_size - 1,
+ *   block_tables[r][0:W] = block_table[r] (row stride bt_row_stride),
+ * exactly as ModelRunner.prepare_decode (model_runner.py:172-188) and its
+ * graph-input copies (:204-210) leave them, and for B <= r < pad_rows
+ * slot_mapping = -1 and context_lens = 0 (the padding rows of a captured
+ * batch). Any output pointer may be NULL (not written). A record that
+ * cannot give a slot (table_len outside [1, W], num_tokens < 1 or beyond
+ * the table, a negative block id) gets slot -1 and sets
+ * NVATTN_STATUS_BAD_SLOT.
+ */
+NVATTN_API size_t nvattn_decode_prepare_bytes(int64_t num_seqs, int32_t table_width);
+
+NVATTN_API int nvattn_decode_prepare(const void* packed_host, void* packed_dev, int64_t num_seqs,
+                                     int32_t table_width, int32_t block_size, int64_t pad_rows,
+                                     int64_t* input_ids, int64_t* positions,
+                                     int32_t* slot_mapping, int32_t* context_lens,
+                                     int32_t* block_tables, int64_t bt_row_stride,
+                                     int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

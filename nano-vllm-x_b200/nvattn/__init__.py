@@ -8,7 +8,8 @@ the in-tree ``libnvattn.so`` (C ABI: include/nvattn.h); build it with
 """
 from .attention import Attention
 from .context import Context, get_context, reset_context, set_context
-from . import ops, tree, parallel
+from . import ops, tree, parallel, decode_meta
+from .decode_meta import DecodeMetadata
 from .ops import (flash_attn_varlen_func, flash_attn_with_kvcache, kv_move, paged_decode,
                   qk_norm_rope_store, sample, sample_merge, sample_shard, store_kvcache,
                   tree_attention, varlen_prefill)
@@ -17,7 +18,7 @@ __all__ = [
     "Attention", "Context", "get_context", "set_context", "reset_context", "ops", "tree",
     "parallel", "store_kvcache", "varlen_prefill", "paged_decode", "tree_attention", "kv_move",
     "flash_attn_varlen_func", "flash_attn_with_kvcache", "qk_norm_rope_store", "sample",
-    "sample_shard", "sample_merge", "install",
+    "sample_shard", "sample_merge", "DecodeMetadata", "decode_meta", "install",
 ]
 
 

@@ -25,7 +25,11 @@ The engine is used unchanged except for what this environment lacks:
   token with nvattn's sampler kernel (``nvattn.ops.sample``); at TP > 1 the
   LM head no longer gathers its logits to rank 0 (embed_head.py:62-65):
   every rank picks within its own vocabulary shard and the ranks exchange
-  one 64-bit key per row (``nvattn.parallel.sample_vocab_parallel``);
+  one 64-bit key per row (``nvattn.parallel.sample_vocab_parallel``); and
+  each decode step's metadata comes from one packed host record and one
+  kernel writing the CUDA graph's inputs in place
+  (``nvattn.DecodeMetadata``, replacing prepare_decode and run_model's
+  copies, model_runner.py:172-188, 204-210);
   ``--attn reference`` keeps the engine's own flash-attn / Triton path.
 
     python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz]
@@ -161,6 +165,53 @@ def _make_runner_class():
             self._sample_step = 0
             patch_engine(self._attn)
             super().__init__(config, rank, event)
+
+        def prepare_decode(self, seqs):
+            """ModelRunner.prepare_decode (model_runner.py:172-188). In the
+            fused arm: one packed record, one copy, one kernel; on the graph
+            path the kernel writes the graph's static inputs directly, so
+            run_model only replays."""
+            if self._attn != "nvattn-fused":
+                return super().prepare_decode(seqs)
+            from nanovllm.utils.context import set_context
+            from nvattn.decode_meta import DecodeMetadata
+            dev = torch.device("cuda", torch.cuda.current_device())
+            if getattr(self, "_decode_meta", None) is None:
+                max_w = (self.config.max_model_len + self.block_size - 1) // self.block_size
+                self._decode_meta = DecodeMetadata(max(self.config.max_num_seqs, 512), max_w,
+                                                   self.block_size, dev)
+            meta = self._decode_meta
+            B, W = meta.pack(seqs)
+            gv = getattr(self, "graph_vars", None)
+            if self.enforce_eager or B > 512 or gv is None:
+                ids = torch.empty(B, dtype=torch.int64, device=dev)
+                pos = torch.empty(B, dtype=torch.int64, device=dev)
+                slots = torch.empty(B, dtype=torch.int32, device=dev)
+                lens = torch.empty(B, dtype=torch.int32, device=dev)
+                tables = torch.empty(B, W, dtype=torch.int32, device=dev)
+                meta.launch(B, input_ids=ids, positions=pos, slot_mapping=slots,
+                            context_lens=lens, block_tables=tables)
+                set_context(False, slot_mapping=slots, context_lens=lens, block_tables=tables)
+                return ids, pos
+            meta.launch(gv["slot_mapping"].numel(), input_ids=gv["input_ids"],
+                        positions=gv["positions"], slot_mapping=gv["slot_mapping"],
+                        context_lens=gv["context_lens"], block_tables=gv["block_tables"])
+            self._graph_inputs_ready = True
+            set_context(False, slot_mapping=gv["slot_mapping"][:B],
+                        context_lens=gv["context_lens"][:B],
+                        block_tables=gv["block_tables"][:B, :W])
+            return gv["input_ids"][:B], gv["positions"][:B]
+
+        @torch.inference_mode()
+        def run_model(self, input_ids, positions, is_prefill):
+            """ModelRunner.run_model (model_runner.py:196-212); the graph's
+            inputs are already in place when prepare_decode wrote them."""
+            if is_prefill or not getattr(self, "_graph_inputs_ready", False):
+                return super().run_model(input_ids, positions, is_prefill)
+            self._graph_inputs_ready = False
+            bs = input_ids.size(0)
+            self.graphs[next(x for x in self.graph_bs if x >= bs)].replay()
+            return self.model.compute_logits(self.graph_vars["outputs"][:bs])
 
         def run(self, seqs, is_prefill):
             """ModelRunner.run (model_runner.py:214-220); in the fused arm at

@@ -235,6 +235,29 @@ def prepare_decode_metadata(seqs, block_size: int):
     return np.array(slots, np.int32), np.array(lens, np.int32), tables
 
 
+def decode_graph_inputs(seqs, block_size: int, pad_rows: int, previous: dict) -> dict:
+    """The decode graph's static inputs after one step: ModelRunner.prepare_decode
+    (model_runner.py:172-188) followed by run_model's copies (:204-210), with
+    pad_rows = the graph's batch rows (the fill_ and zero_ cover them all).
+
+    seqs: dicts with ``last_token``, ``num_tokens`` and ``block_table``.
+    previous: the buffers' contents before the step (``input_ids``,
+    ``positions``, ``slot_mapping``, ``context_lens`` of >= pad_rows rows and
+    a 2-D ``block_tables``); what the reference does not write keeps them.
+    """
+    out = {k: np.array(v, copy=True) for k, v in previous.items()}
+    B = len(seqs)
+    slots, lens, tables = prepare_decode_metadata(seqs, block_size)
+    out["input_ids"][:B] = [s["last_token"] for s in seqs]          # :178, :204
+    out["positions"][:B] = lens.astype(np.int64) - 1                 # :179, :205
+    out["slot_mapping"][:pad_rows] = -1                              # :206
+    out["slot_mapping"][:B] = slots                                  # :207
+    out["context_lens"][:pad_rows] = 0                               # :208
+    out["context_lens"][:B] = lens                                   # :209
+    out["block_tables"][:B, :tables.shape[1]] = tables               # :210
+    return out
+
+
 def padded_block_tables(tables):
     """model_runner.py:123-127: pad rows with -1 to the longest table."""
     width = max(len(t) for t in tables)

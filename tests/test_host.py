@@ -94,6 +94,23 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     assert lib.nvattn_sample_merge(fake, 2, 4, fake, None) == _lib.ERR_INVALID
     assert b"in place" in lib.nvattn_last_error()
     assert lib.nvattn_sample_merge(None, 2, 0, None, None) == _lib.OK
+    # decode-step metadata
+    assert lib.nvattn_decode_prepare_bytes(256, 16) == 256 * (16 + 64)
+    assert lib.nvattn_decode_prepare_bytes(-1, 16) == 0
+    assert lib.nvattn_decode_prepare(None, fake, 4, 2, 256, 3, None, None, None, None, None, 0,
+                                     None, None) == _lib.ERR_INVALID       # pad_rows < seqs
+    assert lib.nvattn_decode_prepare(None, fake, 4, 0, 256, 4, None, None, None, None, None, 0,
+                                     None, None) == _lib.ERR_INVALID       # no block table
+    assert lib.nvattn_decode_prepare(None, fake, 4, 2, 0, 4, None, None, None, None, None, 0,
+                                     None, None) == _lib.ERR_INVALID       # block_size 0
+    assert lib.nvattn_decode_prepare(None, fake, 4, 8, 256, 4, None, None, None, None, fake, 4,
+                                     None, None) == _lib.ERR_INVALID       # table stride < width
+    assert lib.nvattn_decode_prepare(None, None, 4, 2, 256, 4, None, None, None, None, None, 0,
+                                     None, None) == _lib.ERR_INVALID       # no packed record
+    assert lib.nvattn_decode_prepare(None, ctypes.c_void_p(0x1004), 4, 2, 256, 4, None, None, None,
+                                     None, None, 0, None, None) == _lib.ERR_INVALID  # misaligned
+    assert lib.nvattn_decode_prepare(None, None, 0, 0, 256, 0, None, None, None, None, None, 0,
+                                     None, None) == _lib.OK
 
 
 def test_python_wrapper_raises_through_error_path():
@@ -194,7 +211,7 @@ def test_head_shard_matches_engine_split():
 def test_package_surface():
     for name in ("Attention", "store_kvcache", "flash_attn_varlen_func",
                  "flash_attn_with_kvcache", "tree_attention", "kv_move", "qk_norm_rope_store",
-                 "sample", "sample_shard", "sample_merge", "install"):
+                 "sample", "sample_shard", "sample_merge", "DecodeMetadata", "install"):
         assert hasattr(nvattn, name)
     a = nvattn.Attention(16, 128, 128 ** -0.5, 8)
     assert a.k_cache.numel() == 0 and hasattr(a, "v_cache")
