@@ -5,7 +5,7 @@ nanovllm/layers/attention.py:67-74); it has no CPU path, so its outputs are
 recorded on the GPU box by calling flash-attn exactly as the reference does,
 on the seeded cases of ``cases.py``:
 
-    python tests/golden/make_flash_attn_golden.py --out gpurun_out/flash_attn_golden.npz
+    python tests/golden/make_flash_attn_golden.py --out flash_attn_golden.npz
 
 The resulting npz (bf16 outputs as uint16 bit patterns, plus the flash-attn
 version) is committed as tests/golden/flash_attn_golden.npz. If flash-attn
