@@ -37,6 +37,12 @@ replaces (nanovllm/layers/attention.py):
   race picks token i with exactly that probability) and argmax for greedy
   decoding; ``philox4x32_10`` / ``sample_uniforms`` restate the counter-based
   generator the CUDA sampler draws its noise from (Salmon et al., SC 2011).
+* ``pick_keys`` / ``greedy_shard_keys`` / ``merge_pick_keys`` — sampling over
+  vocabulary shards (embed_head.py:17-23, 56-66): per-shard pick keys whose
+  maximum over the shards is the pick on the gathered row.
+* ``prepare_decode_metadata`` / ``decode_graph_inputs`` — ModelRunner's
+  decode metadata (model_runner.py:172-188) and what the decode graph's
+  inputs hold after run_model's copies (model_runner.py:204-210).
 
 All attention math is float32 on torch CPU tensors (inputs are bf16); the
 result is float32 so tests can state their tolerance against it.
