@@ -34,6 +34,13 @@
  *
  *   prepare_decode + graph_vars copies           -> nvattn_decode_prepare
  *
+ * and one for the collective next to attention, the all-reduce of the
+ * row-parallel linears (o_proj, down_proj; linear.py:152-155), for
+ * decode-sized messages:
+ *
+ *   dist.all_reduce(y) of RowParallelLinear      -> nvattn_allreduce
+ *     (+ nvattn_ar_buffer_bytes / _alloc / _open / _close / _free)
+ *
  * Conventions (all entry points):
  *   - Pointers are device pointers unless stated otherwise; no torch types.
  *   - Strides are in ELEMENTS (like torch.Tensor.stride()).
@@ -367,6 +374,37 @@ NVATTN_API int nvattn_decode_prepare(const void* packed_host, void* packed_dev, 
                                      int32_t* slot_mapping, int32_t* context_lens,
                                      int32_t* block_tables, int64_t bt_row_stride,
                                      int32_t* status, void* stream);
+
+/*
+ * One-shot all-reduce (sum) of bf16 partials over NVLink peer memory, for
+ * the dist.all_reduce of RowParallelLinear.forward (linear.py:152-155).
+ *
+ * Set-up, once per process (not per step): each rank allocates one buffer of
+ * nvattn_ar_buffer_bytes(capacity_elems) with nvattn_ar_alloc (zeroed; it
+ * returns the 64-byte CUDA IPC handle), the ranks exchange handles, and each
+ * rank opens its peers' with nvattn_ar_open. The data region of a buffer
+ * starts 4096 bytes after its base.
+ *
+ * Per call: the rank's partial (num_elems bf16) must already be in its own
+ * data region, written by earlier work on `stream`. buffers[p] is rank p's
+ * buffer as mapped in this process (own buffer at [rank]). Every rank of
+ * the group must make the same sequence of calls. out (16-byte aligned, not
+ * in the shared buffer) receives the sum over ranks, accumulated in fp32 in
+ * rank order from rank 0's value and rounded once to bf16: the same bits on
+ * every rank (with two ranks, the single rounded add of NCCL's bf16 sum).
+ * The call returns once every rank has read every partial, so the partial
+ * may be rewritten by the next kernel on the stream. Waits on peers are
+ * bounded (~1 s): on expiry NVATTN_STATUS_TIMEOUT is set and the kernel
+ * finishes. Graph-capturable: the launch count lives in the buffer header.
+ */
+NVATTN_API size_t nvattn_ar_buffer_bytes(int64_t capacity_elems);
+NVATTN_API int nvattn_ar_alloc(size_t bytes, void** buffer, void* ipc_handle);
+NVATTN_API int nvattn_ar_open(const void* ipc_handle, void** peer_buffer);
+NVATTN_API int nvattn_ar_close(void* peer_buffer);
+NVATTN_API int nvattn_ar_free(void* buffer);
+NVATTN_API int nvattn_allreduce(const uint64_t* buffers, int32_t rank, int32_t world,
+                                int64_t num_elems, int64_t capacity_elems, void* out,
+                                int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -29,7 +29,10 @@ The engine is used unchanged except for what this environment lacks:
   each decode step's metadata comes from one packed host record and one
   kernel writing the CUDA graph's inputs in place
   (``nvattn.DecodeMetadata``, replacing prepare_decode and run_model's
-  copies, model_runner.py:172-188, 204-210);
+  copies, model_runner.py:172-188, 204-210); with ``--oneshot-allreduce``
+  (off by default: slower than NCCL so far) the row-parallel linears'
+  all-reduce at TP > 1 runs through nvattn's one-shot peer-memory kernel
+  (``nvattn.allreduce``, linear.py:152-155) for decode-sized messages;
   ``--attn reference`` keeps the engine's own flash-attn / Triton path.
 
     python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz]
@@ -130,6 +133,25 @@ def _lm_head_local_forward(self, x):
     return F.linear(x, self.weight)
 
 
+_ONESHOT = None
+_ONESHOT_CAPACITY = 512 * 4096  # decode graphs up to 512 tokens x hidden 4096
+
+
+def _row_parallel_oneshot_forward(self, x):
+    """RowParallelLinear.forward (linear.py:152-155) at TP > 1 through
+    nvattn's one-shot peer-memory all-reduce; messages larger than its buffer
+    keep the reference's F.linear + dist.all_reduce."""
+    global _ONESHOT
+    if self.tp_size == 1:
+        return self._reference_forward(x)
+    if _ONESHOT is None:  # first call: warm-up, all ranks together, outside capture
+        from nvattn.allreduce import OneShotAllReduce
+        _ONESHOT = OneShotAllReduce(_ONESHOT_CAPACITY)
+    from nvattn.allreduce import row_parallel_forward
+    y = row_parallel_forward(_ONESHOT, x, self.weight, self.bias, self.tp_rank)
+    return y if y is not None else self._reference_forward(x)
+
+
 def patch_engine(attn: str) -> None:
     """Apply the substitutions listed in the module docstring (idempotent)."""
     import nanovllm.engine.llm_engine as llm_engine
@@ -145,7 +167,12 @@ def patch_engine(attn: str) -> None:
         nvattn.install(fuse_qk_norm_rope=(attn == "nvattn-fused"))
     if attn == "nvattn-fused":
         import nanovllm.layers.embed_head as embed_head
+        import nanovllm.layers.linear as linear
         embed_head.ParallelLMHead.forward = _lm_head_local_forward
+        if os.environ.get("NVATTN_E2E_ONESHOT_AR") == "1":
+            if not hasattr(linear.RowParallelLinear, "_reference_forward"):
+                linear.RowParallelLinear._reference_forward = linear.RowParallelLinear.forward
+            linear.RowParallelLinear.forward = _row_parallel_oneshot_forward
 
 
 def _runner_base():
@@ -255,8 +282,10 @@ def bench_workload(num_seqs: int = 256, max_input_len: int = 1024, max_output_le
 
 
 def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: int,
-        enforce_eager: bool, model_dir: str | None = None, out: str | None = None) -> dict:
+        enforce_eager: bool, model_dir: str | None = None, out: str | None = None,
+        oneshot_allreduce: bool = False) -> dict:
     os.environ["NVATTN_E2E_ATTN"] = attn
+    os.environ["NVATTN_E2E_ONESHOT_AR"] = "1" if oneshot_allreduce else "0"
     import nanovllm.engine.llm_engine as llm_engine  # noqa: F401  (reference)
     global E2EModelRunner
     E2EModelRunner = _make_runner_class()
@@ -281,7 +310,7 @@ def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: i
            "output_tokens": total, "seconds": round(dt, 3), "value": round(total / dt, 1),
            "unit": "tok/s", "enforce_eager": enforce_eager,
            "model": "random-init Qwen3-0.6B (28 layers, 16Q/8KV, d128, vocab 151936, bf16)",
-           "decoding": "greedy"}
+           "decoding": "greedy", "oneshot_allreduce": oneshot_allreduce}
     if out:
         np.savez_compressed(out, **{f"r{i}": np.array(o["token_ids"], np.int32)
                                     for i, o in enumerate(outs)})
@@ -306,13 +335,16 @@ def main() -> None:
     ap.add_argument("--model-dir", default=None, help="reuse a written model directory")
     ap.add_argument("--write-model", default=None, help="only write the model to this dir")
     ap.add_argument("--out", default=None, help="save generated token ids (npz)")
+    ap.add_argument("--oneshot-allreduce", action="store_true",
+                    help="fused arm at TP > 1: row-parallel all-reduce through nvattn's "
+                         "peer-memory kernel instead of NCCL")
     args = ap.parse_args()
     if args.write_model:
         Path(args.write_model).mkdir(parents=True, exist_ok=True)
         write_model(Path(args.write_model))
         return
     res = run(args.tp, args.attn, args.num_seqs, args.max_input_len, args.max_output_len,
-              args.enforce_eager, args.model_dir, args.out)
+              args.enforce_eager, args.model_dir, args.out, args.oneshot_allreduce)
     print(json.dumps(res), flush=True)
 
 

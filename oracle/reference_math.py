@@ -40,6 +40,8 @@ replaces (nanovllm/layers/attention.py):
 * ``pick_keys`` / ``greedy_shard_keys`` / ``merge_pick_keys`` — sampling over
   vocabulary shards (embed_head.py:17-23, 56-66): per-shard pick keys whose
   maximum over the shards is the pick on the gathered row.
+* ``allreduce_sum`` — the sum of RowParallelLinear's partials over ranks
+  (dist.all_reduce at linear.py:155) in a fixed order.
 * ``prepare_decode_metadata`` / ``decode_graph_inputs`` — ModelRunner's
   decode metadata (model_runner.py:172-188) and what the decode graph's
   inputs hold after run_model's copies (model_runner.py:204-210).
@@ -262,6 +264,19 @@ def decode_graph_inputs(seqs, block_size: int, pad_rows: int, previous: dict) ->
     out["context_lens"][:B] = lens                                   # :209
     out["block_tables"][:B, :tables.shape[1]] = tables               # :210
     return out
+
+
+def allreduce_sum(partials_bits: np.ndarray) -> np.ndarray:
+    """Sum of bf16 partials over ranks, (world, n) uint16 bit patterns ->
+    (n,) uint16: what dist.all_reduce(y) leaves in y (linear.py:155), restated
+    with a fixed order: fp32 accumulation in rank order from rank 0's value,
+    one round-to-nearest-even to bf16. With two ranks this is the single
+    rounded bf16 add of NCCL's sum."""
+    x = bf16_bits_to_f32(np.asarray(partials_bits, np.uint16))
+    acc = x[0].astype(np.float32).copy()
+    for p in range(1, x.shape[0]):
+        acc = (acc + x[p]).astype(np.float32)
+    return f32_to_bf16_bits(acc)
 
 
 def padded_block_tables(tables):

@@ -94,6 +94,22 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     assert lib.nvattn_sample_merge(fake, 2, 4, fake, None) == _lib.ERR_INVALID
     assert b"in place" in lib.nvattn_last_error()
     assert lib.nvattn_sample_merge(None, 2, 0, None, None) == _lib.OK
+    # one-shot all-reduce: argument checks before any launch
+    import ctypes as C
+    bufs = (C.c_uint64 * 2)(0x10000, 0x20000)
+    assert lib.nvattn_ar_buffer_bytes(1000) == 4096 + 2000
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 0, 8, 8, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 2, 2, 8, 8, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 9, 8, 8, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 9, 8, fake, None, None) == _lib.ERR_INVALID
+    bad = (C.c_uint64 * 2)(0x10000, 0x20008)
+    assert lib.nvattn_allreduce(C.addressof(bad), 0, 2, 8, 8, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 8, 8, C.c_void_p(0x10000 + 4096), None,
+                                None) == _lib.ERR_INVALID            # out inside the shared buffer
+    assert b"overlaps" in lib.nvattn_last_error()
+    assert lib.nvattn_ar_alloc(10, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_ar_open(None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_ar_close(None) == _lib.OK and lib.nvattn_ar_free(None) == _lib.OK
     # decode-step metadata
     assert lib.nvattn_decode_prepare_bytes(256, 16) == 256 * (16 + 64)
     assert lib.nvattn_decode_prepare_bytes(-1, 16) == 0

@@ -238,3 +238,20 @@ def test_vocab_shard_keys_merge_to_the_gathered_argmax():
     k = R.pick_keys(np.array([1.0, 1.0, 2.0, -0.0, 0.0, -np.inf, np.nan], np.float32),
                     np.array([5, 3, 9, 1, 2, 0, 0]))
     assert k[1] > k[0] and k[2] > k[1] and k[3] > k[4] and k[5] == 0 and k[6] == 0
+
+
+def test_allreduce_oracle_is_the_rounded_fp32_sum():
+    """Two ranks: one rounded bf16 add, as torch (and NCCL's bf16 sum) gives;
+    more ranks: fp32 accumulation in rank order, rounded once."""
+    g = torch.Generator().manual_seed(3)
+    parts = (torch.randn(4, 5000, generator=g) * 10).bfloat16()
+    parts[0, :4] = torch.tensor([-0.0, 0.0, float("inf"), 1.0])
+    parts[1, :4] = torch.tensor([-0.0, -0.0, 1.0, float("nan")])
+    bits = parts.view(torch.int16).numpy().view(np.uint16)
+    two = R.allreduce_sum(bits[:2])
+    want2 = (parts[0].float() + parts[1].float()).bfloat16().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(two[4:], want2[4:])
+    assert two[0] == 0x8000 and two[1] == 0x0000 and two[2] == 0x7F80 and np.isnan(R.bf16_bits_to_f32(two[3:4]))[0]
+    four = R.allreduce_sum(bits)
+    acc = parts[0].float() + parts[1].float() + parts[2].float() + parts[3].float()
+    assert np.array_equal(four[4:], acc.bfloat16().view(torch.int16).numpy().view(np.uint16)[4:])
