@@ -14,6 +14,9 @@ on a machine without the CUDA library these functions raise.
     qk_norm_rope_store       q/k RMSNorm + rotary + scatter, the steps of
                              Qwen3Attention.forward at qwen3.py:82-86
     sample                   Sampler.forward (sampler.py:5-12) / greedy argmax
+    sample_shard,            the same pick per vocabulary shard and the merge
+    sample_merge             of the shards' keys, in place of ParallelLMHead's
+                             logits gather at TP > 1 (embed_head.py:56-66)
 
 Every launch is asynchronous on ``torch.cuda.current_stream()``, performs
 no host synchronisation and allocates only through torch's caching
@@ -36,6 +39,8 @@ __all__ = [
     "kv_move",
     "qk_norm_rope_store",
     "sample",
+    "sample_shard",
+    "sample_merge",
     "decode_workspace_bytes",
     "tree_workspace_bytes",
     "status_tensor",
