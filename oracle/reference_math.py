@@ -21,7 +21,9 @@ replaces (nanovllm/layers/attention.py):
   j % block_size of block block_table[b, j // block_size].
 * ``decode_attention``    — flash_attn_with_kvcache at attention.py:72-74:
   one query per sequence over cache_seqlens[b] cached keys (causal is moot
-  for a single query); cache_seqlens == 0 gives 0.
+  for a single query); cache_seqlens == 0 gives 0. ``decode_attention_c`` is
+  the same function restated in C with OpenMP (oracle/decode_ref.c), the
+  timed CPU baseline.
 * ``tree_attention``      — no reference code: the ancestor-mask definition
   (a node sees the whole committed context plus the tree nodes whose bits
   are set in its mask word).
@@ -166,6 +168,42 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         kb = gather_paged(k_cache, block_table[b], n)
         vb = gather_paged(v_cache, block_table[b], n)
         out[b:b + 1] = _attend(q[b:b + 1], kb, vb, scale, None)
+    return out
+
+
+_C_DECODE = None
+
+
+def decode_attention_c(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                       cache_seqlens, block_table, scale: float,
+                       threads: int | None = None) -> torch.Tensor:
+    """decode_attention through the C restatement (oracle/decode_ref.c, OpenMP
+    over (sequence, KV head) pairs): the same function, for the timed CPU
+    baseline. Needs oracle/liboracle_decode.so (oracle/build_oracle.py)."""
+    global _C_DECODE
+    import ctypes
+    import os
+    from pathlib import Path
+    if _C_DECODE is None:
+        lib = ctypes.CDLL(str(Path(__file__).resolve().parent / "liboracle_decode.so"))
+        f = lib.oracle_decode_attention
+        f.restype = ctypes.c_int
+        f.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 6 + [ctypes.c_float,
+                                                                      ctypes.c_void_p, ctypes.c_int]
+        _C_DECODE = f
+    B, H, D = q.shape
+    KVH, bs = k_cache.shape[2], k_cache.shape[1]
+    qc = q.contiguous().view(torch.int16)
+    kc = k_cache.contiguous().view(torch.int16)
+    vc = v_cache.contiguous().view(torch.int16)
+    lens = np.ascontiguousarray(cache_seqlens, dtype=np.int32)
+    bt = np.ascontiguousarray(block_table, dtype=np.int32)
+    out = torch.empty(B, H, D, dtype=torch.float32)
+    rc = _C_DECODE(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.ctypes.data, bt.ctypes.data,
+                   B, H, KVH, D, bs, bt.shape[1], scale, out.data_ptr(),
+                   threads or os.cpu_count() or 1)
+    if rc != 0:
+        raise ValueError("oracle_decode_attention: unsupported sizes or a length past its table")
     return out
 
 

@@ -255,3 +255,28 @@ def test_allreduce_oracle_is_the_rounded_fp32_sum():
     four = R.allreduce_sum(bits)
     acc = parts[0].float() + parts[1].float() + parts[2].float() + parts[3].float()
     assert np.array_equal(four[4:], acc.bfloat16().view(torch.int16).numpy().view(np.uint16)[4:])
+
+
+def test_c_decode_restatement_matches_the_torch_oracle():
+    """oracle/decode_ref.c (the timed CPU baseline) against decode_attention:
+    GQA groups of 1, 2 and 8, empty sequences, permuted paged tables."""
+    import sys
+    sys.path.insert(0, str(GOLDEN.parents[1] / "oracle"))
+    from build_oracle import build_c_oracle
+    build_c_oracle()
+    g = torch.Generator().manual_seed(9)
+    for H, KVH, bs in ((8, 8, 16), (16, 8, 256), (64, 8, 64)):
+        lens = np.array([0, 1, 37, 300, 513], np.int32)
+        W = int((lens.max() + bs - 1) // bs) + 1
+        nb = len(lens) * W
+        perm = np.random.default_rng(H).permutation(nb).astype(np.int32)
+        bt = perm.reshape(len(lens), W)
+        kc = torch.randn(nb, bs, KVH, 128, generator=g).bfloat16()
+        vc = torch.randn(nb, bs, KVH, 128, generator=g).bfloat16()
+        q = torch.randn(len(lens), H, 128, generator=g).bfloat16()
+        want = R.decode_attention(q, kc, vc, lens, bt, 128 ** -0.5)
+        got = R.decode_attention_c(q, kc, vc, lens, bt, 128 ** -0.5)
+        assert torch.allclose(got, want, atol=2e-5, rtol=1e-4), (H, (got - want).abs().max())
+        assert got[0].abs().max() == 0
+    with pytest.raises(ValueError):
+        R.decode_attention_c(q, kc, vc, np.array([W * bs + 1] + [1] * 4, np.int32), bt, 1.0)
