@@ -31,7 +31,7 @@ class _Rank:
         self.data = np.zeros(n, np.int64)
 
 
-def _wait(cond, limit=5.0):
+def _wait(cond, limit=30.0):
     t0 = time.monotonic()
     while not cond():
         if time.monotonic() - t0 > limit:
