@@ -166,9 +166,25 @@ def dist_setup(n_gpus: int):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        _gloo_group()  # collective: every rank creates it here, in the same order
     else:
         torch.cuda.set_device(0)
     return rank, world, local
+
+
+_GLOO = None
+
+
+def _gloo_group():
+    """A CPU process group with a long timeout, for ranks that wait while rank 0
+    runs the end-to-end engine (minutes)."""
+    global _GLOO
+    if _GLOO is None:
+        import datetime
+
+        import torch.distributed as dist
+        _GLOO = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=3600))
+    return _GLOO
 
 
 def barrier(world):
@@ -195,6 +211,13 @@ def sum_over_ranks(x: float, world: int, device: str = "cuda") -> float:
     t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
+
+
+def reference_on_path() -> None:
+    """Make the reference package (installed into baseline/_ref) importable."""
+    ref_dir = REPO / "baseline" / "_ref"
+    if ref_dir.is_dir() and str(ref_dir) not in sys.path:
+        sys.path.append(str(ref_dir))
 
 
 # ------------------------------------------------------------- nvattn arm
@@ -340,6 +363,7 @@ def run_nvattn(args):
         secondary["tree_verify_cfg5"] = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
         secondary["qk_norm_rope_store"] = bench_qknorm(dev, rank, world, args, hbm_peak)
         if world == 1:
+            secondary["store_kvcache"] = bench_store_kvcache(dev, args, hbm_peak)
             secondary["sampler"] = bench_sampler(dev, args, hbm_peak)
             try:
                 secondary["layer_cfg0"] = bench_layer_cfg0(dev, args)
@@ -363,6 +387,17 @@ def run_nvattn(args):
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
         cpu = cpu_decode_sample(args.cpu_seconds)
+
+    if not args.skip_e2e:
+        # every rank frees its memory; rank 0 runs the engine at TP = world over all
+        # GPUs while the others wait (a gloo barrier: no NCCL call stays pending)
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        if rank == 0:
+            secondary["e2e_cfg1"] = bench_e2e(args, world)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(group=_gloo_group())
 
     if rank == 0:
         line = {
@@ -445,13 +480,34 @@ def bench_prefill(dev, rank, world, args, tf_peak):
                         world)
     total = sum_over_ranks(flops, world)
     tfs = total / (ms * 1e-3) / 1e12
-    return {"metric": "prefill attn TFLOP/s", "value": round(tfs, 1), "unit": "TFLOP/s",
-            "ms_per_step": round(ms, 4),
-            "frac_of_measured_bf16_peak_per_gpu": round(tfs / world / tf_peak, 4),
-            "frac_of_measured_bf16_sustained_peak_per_gpu": round(tfs / world / load_peaks()[2], 4),
-            "flops_per_step": total,
-            "workload": "configs[2]: 64 seqs, 2048-token shared prefix (8 blocks), suffix "
-                        "U[128,512], 32Q/8KV, d128, causal over prefix+suffix"}
+    res = {"metric": "prefill attn TFLOP/s", "value": round(tfs, 1), "unit": "TFLOP/s",
+           "ms_per_step": round(ms, 4),
+           "frac_of_measured_bf16_peak_per_gpu": round(tfs / world / tf_peak, 4),
+           "frac_of_measured_bf16_sustained_peak_per_gpu": round(tfs / world / load_peaks()[2], 4),
+           "flops_per_step": total,
+           "workload": "configs[2]: 64 seqs, 2048-token shared prefix (8 blocks), suffix "
+                       "U[128,512], 32Q/8KV, d128, causal over prefix+suffix"}
+    if world == 1:
+        # the reference's own GPU prefill on the same cache: flash_attn_varlen_func as
+        # attention.py:64-70 calls it on a prefix-cache hit (block_table set)
+        try:
+            from flash_attn import flash_attn_varlen_func
+
+            def fa():
+                flash_attn_varlen_func(q, kc, vc, max_seqlen_q=int(suf.max()), cu_seqlens_q=cq,
+                                       max_seqlen_k=int(klen.max()), cu_seqlens_k=ck,
+                                       softmax_scale=D ** -0.5, causal=True, block_table=btd)
+
+            for _ in range(args.warmup):
+                fa()
+            ms_fa = timed(fa, args.steps, torch.cuda.current_stream(dev)) / args.steps
+            res["flash_attn_varlen_func"] = {
+                "impl": "flash-attn (reference GPU path, attention.py:64-70)",
+                "value": round(flops / (ms_fa * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                "ms_per_step": round(ms_fa, 4)}
+        except Exception as e:  # noqa: BLE001  (a comparison line never sinks the bench)
+            res["flash_attn_varlen_func"] = {"unavailable": f"{e!r}"[:200]}
+    return res
 
 
 def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
@@ -530,6 +586,153 @@ def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
                 "frac_of_measured_hbm_per_gpu": round(
                     sum_over_ranks(nbytes_l, world) / (ms_l * 1e-3) / 1e9 / world / hbm_peak, 4),
                 "workload": "same 32 contexts, 8-token n-gram chain per sequence"}}
+
+
+def bench_store_kvcache(dev, args, hbm_peak):
+    """The KV scatter alone (attention.py:10-40) at the Qwen3-0.6B shape
+    (8 KV heads, d128, 256-token blocks): a 16,384-token prefill chunk
+    (max_num_batched_tokens; slots in runs of whole blocks, blocks permuted,
+    as prepare_prefill lays them out) and a 256-row decode batch (one random
+    slot per sequence). K and V are strided views of a qkv projection
+    (16Q/8KV), as Qwen3Attention passes them. Beside it the reference's own
+    Triton kernel (store_kvcache) on the same inputs."""
+    from nvattn import ops
+    reference_on_path()
+    try:
+        from nanovllm.layers.attention import store_kvcache as ref_store
+    except Exception as e:  # noqa: BLE001
+        ref_store, ref_err = None, f"reference package not importable: {e!r}"[:200]
+    H, KVH = 16, 8
+    g = torch.Generator(device=dev).manual_seed(31)
+    res = {"metric": "store_kvcache GB/s", "unit": "GB/s",
+           "bytes": "2*N*KVH*d*2 read + the same written + 4N of slots",
+           "timing": "10 calls per CUDA graph, device time per call (both implementations); "
+                     "4 input sets and caches in turn (prefill: 4 x 201 MB, larger than L2)"}
+    for name, n in (("prefill_chunk_16384", 16384), ("decode_batch_256", 256)):
+        nb = max(64, (n + BS - 1) // BS * 2)
+        sets = []
+        for _ in range(4):
+            qkv = torch.randn(n, (H + 2 * KVH) * D, generator=g, device=dev).to(torch.bfloat16)
+            _, k, v = qkv.split([H * D, KVH * D, KVH * D], dim=-1)
+            k, v = k.view(n, KVH, D), v.view(n, KVH, D)
+            kc = torch.zeros(nb, BS, KVH, D, dtype=torch.bfloat16, device=dev)
+            vc = torch.zeros_like(kc)
+            if n >= BS:
+                blocks = torch.randperm(nb, generator=g, device=dev)[:(n + BS - 1) // BS]
+                slots = (blocks[:, None] * BS + torch.arange(BS, device=dev)[None]).flatten()[:n]
+            else:
+                slots = torch.randperm(nb * BS, generator=g, device=dev)[:n]
+            sets.append((qkv, k, v, kc, vc, slots.to(torch.int32)))
+        nbytes = float(2 * n * KVH * D * 2 * 2 + 4 * n)
+        turn = [0]
+
+        def nxt():
+            turn[0] = (turn[0] + 1) % len(sets)
+            return sets[turn[0]]
+
+        def nv_fn():
+            _, k, v, kc, vc, sl = nxt()
+            ops.store_kvcache(k, v, kc, vc, sl)
+
+        for _ in range(args.warmup):
+            nv_fn()
+        ms = graph_timed(nv_fn, args.steps, dev)
+        row = {"value": round(nbytes / (ms * 1e-3) / 1e9, 1), "us_per_call": round(ms * 1e3, 2),
+               "frac_of_measured_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+               "bytes_per_call": nbytes}
+        if ref_store is None:
+            row["reference_triton"] = {"unavailable": ref_err}
+        else:
+            try:
+                def ref_fn():
+                    _, k, v, kc, vc, sl = nxt()
+                    ref_store(k, v, kc, vc, sl)
+
+                for _ in range(max(args.warmup, 3)):
+                    ref_fn()
+                ms_ref = graph_timed(ref_fn, args.steps, dev)
+                row["reference_triton"] = {
+                    "impl": "reference store_kvcache (Triton, attention.py:10-40)",
+                    "value": round(nbytes / (ms_ref * 1e-3) / 1e9, 1),
+                    "us_per_call": round(ms_ref * 1e3, 2)}
+                # both wrote the same caches from the same inputs: check one set bit for bit
+                _, k, v, kc, vc, sl = sets[0]
+                ref_store(k, v, kc, vc, sl)
+                kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+                ops.store_kvcache(k, v, kc2, vc2, sl)
+                kc3, vc3 = torch.zeros_like(kc), torch.zeros_like(vc)
+                ref_store(k, v, kc3, vc3, sl)
+                row["caches_identical_to_reference"] = bool(torch.equal(kc2, kc3) and
+                                                            torch.equal(vc2, vc3))
+            except Exception as e:  # noqa: BLE001
+                row["reference_triton"] = {"unavailable": f"{e!r}"[:200]}
+        res[name] = row
+        del sets
+        torch.cuda.empty_cache()
+    res["value"] = res["prefill_chunk_16384"]["value"]
+    return res
+
+
+def bench_e2e(args, world):
+    """configs[1] end to end (the third part of the metric; the reference's
+    bench.py:8-28 workload through its own engine): nvattn.e2e runs the fused
+    nvattn arm and the reference arm at TP = world size, each in a fresh
+    process, on the full 256-request workload, greedy. Returns tok/s, seconds
+    and the number of requests whose ids are identical between the arms."""
+    import tempfile
+    reference_on_path()
+    try:
+        import nanovllm  # noqa: F401
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference engine not importable: {e!r}"[:200]}
+    env = dict(os.environ)
+    for key in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK",
+                "ROLE_RANK", "MASTER_ADDR", "MASTER_PORT", "TORCHELASTIC_RUN_ID"):
+        env.pop(key, None)  # the engine sets up its own process group
+    env["PYTHONPATH"] = os.pathsep.join([str(REPO / "nano-vllm-x_b200"), str(REPO),
+                                         str(REPO / "baseline" / "_ref"),
+                                         env.get("PYTHONPATH", "")])
+    res = {"metric": "e2e out tok/s", "unit": "tok/s", "tp": world,
+           "workload": "configs[1]: 256 requests (bench.py draw order, random.seed(0)), input and "
+                       "output lengths U[100,1024], ignore_eos, greedy; random-init Qwen3-0.6B, "
+                       "CUDA-graph decode; each arm in a fresh engine process",
+           "timing": "wall clock of llm.generate after one warm-up request (engine set-up and "
+                     "graph capture excluded), as the reference's bench.py times it"}
+    with tempfile.TemporaryDirectory() as tmp:
+        model_dir = Path(tmp) / "model"
+        r = subprocess.run([sys.executable, "-m", "nvattn.e2e", "--write-model", str(model_dir)],
+                           env=env, capture_output=True, text=True, timeout=600)
+        if r.returncode != 0:
+            return dict(res, error=r.stderr[-300:])
+        outs = {}
+        for arm in ("nvattn-fused", "reference"):
+            out = Path(tmp) / f"{arm}.npz"
+            cmd = [sys.executable, "-m", "nvattn.e2e", "--tp", str(world), "--attn", arm,
+                   "--model-dir", str(model_dir), "--out", str(out)]
+            try:
+                r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
+            except subprocess.TimeoutExpired:
+                res[arm] = {"error": "timed out after 900 s"}
+                continue
+            if r.returncode != 0:
+                res[arm] = {"error": r.stderr[-300:]}
+                continue
+            line = json.loads(r.stdout.strip().splitlines()[-1])
+            res[arm] = {"value": line["value"], "seconds": line["seconds"],
+                        "output_tokens": line["output_tokens"]}
+            outs[arm] = out
+        if len(outs) == 2:
+            sys.path.insert(0, str(REPO / "nano-vllm-x_b200"))
+            from nvattn.e2e import compare
+            cmp = compare(str(outs["reference"]), str(outs["nvattn-fused"]))
+            res["identical_requests"] = cmp["identical"]
+            res["requests"] = cmp["requests"]
+            res["median_first_divergence_frac"] = cmp["median_first_divergence_frac"]
+    if "value" in res.get("nvattn-fused", {}):
+        res["value"] = res["nvattn-fused"]["value"]
+    if "value" in res.get("reference", {}) and "value" in res:
+        res["speedup_vs_reference"] = round(res["value"] / res["reference"]["value"], 3)
+    return res
 
 
 def bench_layer_cfg0(dev, args):
@@ -642,9 +845,7 @@ def _reference_qknorm(dev, args, pos, q, k, v, w, cos_sin, kc, vc, slots, nbytes
     """The reference's modules on the same inputs: RMSNorm (layernorm.py:16-26,
     torch.compile), RotaryEmbedding (rotary_embedding.py:37-48, torch.compile)
     and the Triton store_kvcache (attention.py:10-40)."""
-    ref_dir = REPO / "baseline" / "_ref"  # the reference package, when installed there
-    if ref_dir.is_dir() and str(ref_dir) not in sys.path:
-        sys.path.append(str(ref_dir))
+    reference_on_path()
     try:
         from nanovllm.layers.attention import store_kvcache
         from nanovllm.layers.layernorm import RMSNorm
@@ -725,9 +926,7 @@ def bench_sampler(dev, args, hbm_peak):
     ms = graph_timed(shard_fn, args.steps, dev)
     res["tp2_rank_shard_sampled"] = {"value": round(nbytes / 2 / (ms * 1e-3) / 1e9, 1),
                                      "ms_per_step": round(ms, 4)}
-    ref_dir = REPO / "baseline" / "_ref"
-    if ref_dir.is_dir() and str(ref_dir) not in sys.path:
-        sys.path.append(str(ref_dir))
+    reference_on_path()
     try:
         from nanovllm.layers.sampler import Sampler
         sampler = Sampler()
@@ -768,9 +967,7 @@ def bench_decode_prepare(dev, args):
     from types import SimpleNamespace
 
     from nvattn.decode_meta import DecodeMetadata
-    ref_dir = REPO / "baseline" / "_ref"
-    if ref_dir.is_dir() and str(ref_dir) not in sys.path:
-        sys.path.append(str(ref_dir))
+    reference_on_path()
     try:
         from nanovllm.engine.model_runner import ModelRunner
         from nanovllm.engine.sequence import Sequence
@@ -887,16 +1084,12 @@ def _cpu_pool():
     return _POOL
 
 
-def cpu_decode_sample(budget_s: float, max_seqs: int = BATCH):
-    """Oracle decode (the reference's attention math restated on the CPU) over
-    the workload's sequences, in order, until `budget_s` seconds of CPU time
-    or `max_seqs` sequences; all host threads. The oracle's cost does not
-    depend on the values, so one random KV pool is generated once and each
-    sequence reads its first ceil(ctx/256) blocks of it."""
+CPU_SAMPLE_SEQS = 32  # the CPU sample: the workload's first 32 sequences, all heads
+
+
+def _cpu_impl():
     sys.path.insert(0, str(REPO))
     from oracle import reference_math as R
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
     lens, kc, vc, q, bt = _cpu_pool()
     # the C restatement (OpenMP over sequence x KV head) when built, else torch's
     impl, how = R.decode_attention_c, "C restatement (oracle/decode_ref.c), OpenMP"
@@ -904,46 +1097,74 @@ def cpu_decode_sample(budget_s: float, max_seqs: int = BATCH):
         impl(q, kc, vc, np.array([1]), bt, D ** -0.5)
     except OSError:
         impl, how = R.decode_attention, "torch fp32 restatement (oracle)"
+    return impl, how
+
+
+def cpu_decode_pass(impl, nseq: int = CPU_SAMPLE_SEQS):
+    """One oracle decode call over the workload's first `nseq` sequences (all
+    64Q/8KV heads; OpenMP over the nseq x 8 (sequence, KV head) pairs, so every
+    host thread works). The oracle's cost does not depend on the values, so
+    one random KV pool is generated once and every sequence reads its first
+    ceil(ctx/256) blocks of it. Returns (algorithmic KV bytes, seconds)."""
+    lens, kc, vc, q, bt = _cpu_pool()
+    sl = lens[:nseq].astype(np.int32)
+    qb = q.expand(nseq, -1, -1).contiguous()
+    btb = np.repeat(bt, nseq, axis=0)
+    t0 = time.perf_counter()
+    impl(qb, kc, vc, sl, btb, D ** -0.5)
+    dt = time.perf_counter() - t0
+    return int(sl.astype(np.int64).sum()) * KVH_TOTAL * D * 2 * 2, dt
+
+
+def cpu_decode_sample(budget_s: float):
+    """The CPU baseline: passes of cpu_decode_pass over the same sample until
+    `budget_s` seconds of CPU time (at least two); all host threads."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    impl, how = _cpu_impl()
+    cpu_decode_pass(impl, 2)  # warm-up (page in the pool)
     done_bytes, t_total, n = 0, 0.0, 0
-    for b in range(min(BATCH, max_seqs)):
-        L = int(lens[b])
-        t0 = time.perf_counter()
-        impl(q, kc, vc, np.array([L]), bt, D ** -0.5)
-        t_total += time.perf_counter() - t0
-        done_bytes += L * KVH_TOTAL * D * 2 * 2
+    while n < 2 or t_total < budget_s:
+        nb, dt = cpu_decode_pass(impl)
+        done_bytes += nb
+        t_total += dt
         n += 1
-        if t_total > budget_s and n >= 2:
-            break
     return {"value": round(done_bytes / t_total / 1e9, 3), "unit": "GB/s", "cores": threads,
             "kind": "port",
-            "sample": f"{n} of {BATCH} sequences of the workload (all 64Q/8KV heads), "
-                      f"{t_total:.2f} s of CPU time, {how}, {threads} threads"}
+            "sample": f"the workload's first {CPU_SAMPLE_SEQS} of {BATCH} sequences (all "
+                      f"64Q/8KV heads) per pass, {n} passes, {t_total:.2f} s of CPU time, {how}, "
+                      f"{threads} threads"}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return  # the CPU reference runs on rank 0 only
-    # each step: the oracle over the workload's first sequences (a bounded sample)
-    per_step = max(2, min(BATCH, 32))
-    cpu_decode_sample(1.0, 2)  # warm-up
-    vals, last = [], None
-    t0 = time.perf_counter()
+    # each step: one pass of the oracle over the same bounded sample as cpu_baseline
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    impl, how = _cpu_impl()
+    for _ in range(args.warmup):
+        cpu_decode_pass(impl, 2)
+    vals, total_s = [], 0.0
     for _ in range(max(1, args.steps)):
-        last = cpu_decode_sample(args.cpu_seconds, per_step)
-        vals.append(last["value"])
-    value = statistics.median(vals)
+        nb, dt = cpu_decode_pass(impl)
+        vals.append(nb / dt / 1e9)
+        total_s += dt
+    value = round(statistics.median(vals), 3)
+    sample = (f"the workload's first {CPU_SAMPLE_SEQS} of {BATCH} sequences (all 64Q/8KV heads) "
+              f"per step, {how}, {threads} threads")
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round((time.perf_counter() - t0) * 1e3 / max(1, args.steps), 2),
+        "ms_per_step": round(total_s * 1e3 / max(1, args.steps), 2),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "impl": "reference",
         "config": {"workload": WORKLOAD, "global_batch": BATCH, "num_heads": H_TOTAL,
                    "num_kv_heads": KVH_TOTAL, "head_dim": D, "block_size": BS,
                    "parallelism": "cpu (host cores)"},
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": last["cores"],
-                         "kind": "port", "sample": last["sample"]},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -965,6 +1186,14 @@ def run_only(args):
         res = bench_layer_cfg0(dev, args)
     elif args.only == "prep":
         res = bench_decode_prepare(dev, args)
+    elif args.only == "store":
+        res = bench_store_kvcache(dev, args, hbm_peak)
+    elif args.only == "e2e":
+        torch.cuda.empty_cache()
+        res = bench_e2e(args, world) if rank == 0 else None
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(group=_gloo_group())
     else:
         res = bench_tree(dev, rank, world, args, tf_peak, hbm_peak)
     if rank == 0:
@@ -985,10 +1214,13 @@ def main():
                     help="decode batch (configs[3] = 128; smaller values only for ncu captures)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
-    ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler", "layer", "prep"),
+    ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler", "layer", "prep",
+                                       "store", "e2e"),
                     default=None,
                     help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-e2e", action="store_true",
+                    help="leave out the end-to-end generation leg (configs[1])")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -382,20 +382,23 @@ NVATTN_API int nvattn_decode_prepare(const void* packed_host, void* packed_dev, 
  * Set-up, once per process (not per step): each rank allocates one buffer of
  * nvattn_ar_buffer_bytes(capacity_elems) with nvattn_ar_alloc (zeroed; it
  * returns the 64-byte CUDA IPC handle), the ranks exchange handles, and each
- * rank opens its peers' with nvattn_ar_open. The data region of a buffer
- * starts 4096 bytes after its base.
+ * rank opens its peers' with nvattn_ar_open. A buffer is a 4096-byte header
+ * of flags followed by two data halves of capacity_elems bf16 each; calls
+ * alternate between the halves.
  *
- * Per call: the rank's partial (num_elems bf16) must already be in its own
- * data region, written by earlier work on `stream`. buffers[p] is rank p's
- * buffer as mapped in this process (own buffer at [rank]). Every rank of
- * the group must make the same sequence of calls. out (16-byte aligned, not
- * in the shared buffer) receives the sum over ranks, accumulated in fp32 in
- * rank order from rank 0's value and rounded once to bf16: the same bits on
- * every rank (with two ranks, the single rounded add of NCCL's bf16 sum).
- * The call returns once every rank has read every partial, so the partial
- * may be rewritten by the next kernel on the stream. Waits on peers are
- * bounded (~1 s): on expiry NVATTN_STATUS_TIMEOUT is set and the kernel
- * finishes. Graph-capturable: the launch count lives in the buffer header.
+ * Per call: `in` holds the rank's partial (num_elems bf16, written by earlier
+ * work on `stream`); buffers[p] is rank p's buffer as mapped in this process
+ * (own buffer at [rank]). Every rank of the group must make the same sequence
+ * of calls with the same num_elems. out receives the sum over ranks,
+ * accumulated in fp32 in rank order from rank 0's value and rounded once to
+ * bf16: the same bits on every rank (with two ranks, the single rounded add
+ * of NCCL's bf16 sum). in and out are 16-byte aligned, outside the shared
+ * buffer, and may be the same tensor (in place). The kernel copies `in` into
+ * the shared buffer itself, so `in` may be rewritten as soon as the call's
+ * kernel has run. Waits on peers are bounded (about a second by default;
+ * nvattn_ar_set_wait_limit changes it): on expiry NVATTN_STATUS_TIMEOUT is
+ * set, the kernel finishes, and that call's output is not valid.
+ * Graph-capturable: the launch count lives in the buffer header.
  */
 NVATTN_API size_t nvattn_ar_buffer_bytes(int64_t capacity_elems);
 NVATTN_API int nvattn_ar_alloc(size_t bytes, void** buffer, void* ipc_handle);
@@ -403,8 +406,16 @@ NVATTN_API int nvattn_ar_open(const void* ipc_handle, void** peer_buffer);
 NVATTN_API int nvattn_ar_close(void* peer_buffer);
 NVATTN_API int nvattn_ar_free(void* buffer);
 NVATTN_API int nvattn_allreduce(const uint64_t* buffers, int32_t rank, int32_t world,
-                                int64_t num_elems, int64_t capacity_elems, void* out,
-                                int32_t* status, void* stream);
+                                int64_t num_elems, int64_t capacity_elems, const void* in,
+                                void* out, int32_t* status, void* stream);
+/*
+ * Sets the limit, in SM clock cycles, of every later nvattn_allreduce
+ * launch's waits on its peers (a launch captured in a CUDA graph keeps the
+ * limit it was captured with); cycles <= 0 restores the default of 2e9
+ * (about a second). Returns the previous limit. Tests shorten it to see a
+ * wait on a peer that never arrives end with NVATTN_STATUS_TIMEOUT.
+ */
+NVATTN_API int64_t nvattn_ar_set_wait_limit(int64_t cycles);
 
 #ifdef __cplusplus
 }  /* extern "C" */

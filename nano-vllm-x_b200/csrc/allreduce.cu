@@ -2,44 +2,59 @@
 // (replaces the dist.all_reduce of RowParallelLinear.forward,
 // nanovllm/layers/linear.py:152-155, for decode-sized messages).
 //
-// Every rank owns one IPC-shared buffer: a 4 KB header of flags, then the
-// data region. The rank's GEMM writes its partial product into its own data
-// region (local memory only), then one launch of allreduce_oneshot_kernel
+// Every rank owns one IPC-shared buffer: a 4 KB header of flags, then two
+// data halves of `capacity` bf16 each. Launch e (the rank's e-th call)
+// uses half e % 2. The message is cut into one contiguous chunk per block,
+// and block b of every rank handles chunk b:
 //
-//   1. announces "partial of launch e ready" to every rank (a release store
-//      of e into start[rank] of each rank's header) and waits until every
-//      rank has announced e (acquire loads of its own header);
-//   2. sums the partials of all ranks, read over NVLink, in rank order in
-//      fp32 starting from rank 0's value, rounded once to bf16: every rank
-//      computes the same bits, and with two ranks the result is the single
-//      rounded bf16 add that NCCL's bf16 sum gives;
-//   3. when its last block is done, announces "finished reading launch e"
-//      (end[rank] on every rank) and waits for every rank's end flag before
-//      the launch completes, so the next GEMM may overwrite the partial.
+//   1. copies its chunk of this rank's input into half e % 2 of the rank's
+//      own buffer (local memory only);
+//   2. publishes it: a system-scope fence, then a release store of e into
+//      flag[rank][b] of every rank's header (one thread per rank);
+//   3. waits until flag[p][b] of its own header has reached e for every
+//      rank p (acquire loads, bounded);
+//   4. sums chunk b of half e % 2 of every rank's buffer, read over NVLink,
+//      in rank order in fp32 starting from rank 0's value, rounded once to
+//      bf16: every rank computes the same bits, and with two ranks the result
+//      is the single rounded bf16 add that NCCL's bf16 sum gives.
 //
-// The launch count e lives in the header (the last block stores it), so a
-// captured CUDA graph replays correctly. Every wait is bounded: after about
-// a second it records NVATTN_STATUS_TIMEOUT and the kernel finishes.
+// No block waits for another block of its own launch, so nothing depends on
+// the blocks being co-resident. There is no closing barrier: a rank next
+// writes half e % 2 in launch e + 2, which starts after its launch e + 1
+// completed; every block of launch e + 1 waited for every peer's launch-e+1
+// flags, which a peer publishes only after its own launch e (and its reads of
+// half e % 2) completed. The last block to finish records e in the header,
+// so a captured CUDA graph replays correctly. Every wait is bounded: after
+// the wait limit (about a second by default) it records
+// NVATTN_STATUS_TIMEOUT and the kernel finishes; that launch's output is then
+// not valid.
 #include <string.h>
+
+#include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 
 namespace nvattn {
 
 constexpr int kArMaxRanks = 8;
-constexpr int kArThreads = 256;
+constexpr int kArThreads = 512;
+constexpr int kArMaxBlocks = 120;
+constexpr int kArVecsPerThread = 2;  // 16-byte vectors per thread and rank, loads in flight
 constexpr size_t kArHeaderBytes = 4096;
 
 struct ArHeader {
-  uint32_t start[kArMaxRanks];  // start[p]: last launch whose partial rank p announced
-  uint32_t end[kArMaxRanks];    // end[p]: last launch rank p finished reading
-  uint32_t epoch;               // launches this rank has completed
-  uint32_t done;                // blocks of the running launch that have finished
+  uint32_t flag[kArMaxRanks][kArMaxBlocks];  // flag[p][b]: last launch whose chunk b rank p published
+  uint32_t epoch;                            // launches this rank has completed
+  uint32_t done;                             // blocks of the running launch that have finished
 };
+static_assert(sizeof(ArHeader) <= kArHeaderBytes, "all-reduce header exceeds 4 KB");
 
 struct ArPeers {
   char* base[kArMaxRanks];  // each rank's buffer (this rank's own at [rank])
 };
+
+static std::atomic<long long> g_ar_wait_limit{kWaitLimitCycles};
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -51,12 +66,12 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait until *flag has reached e (wrap-safe), at most kWaitLimitCycles.
-__device__ __forceinline__ bool wait_reached(const uint32_t* flag, uint32_t e) {
+// Wait until *flag has reached e (wrap-safe), at most `limit` SM cycles.
+__device__ __forceinline__ bool wait_reached(const uint32_t* flag, uint32_t e, long long limit) {
   const long long t0 = clock64();
   while (static_cast<int32_t>(ld_acquire_sys(flag) - e) < 0) {
-    if (clock64() - t0 > kWaitLimitCycles) return false;
-    __nanosleep(64);
+    if (clock64() - t0 > limit) return false;
+    __nanosleep(32);
   }
   return true;
 }
@@ -109,7 +124,9 @@ __device__ __forceinline__ int4 pack8(const float acc[8]) {
 
 __global__ void __launch_bounds__(kArThreads)
     allreduce_oneshot_kernel(const ArPeers peers, int rank, int world, int64_t n,
-                             __nv_bfloat16* __restrict__ out, int32_t* status) {
+                             int64_t half_bytes, int64_t per_block,
+                             const __nv_bfloat16* in, __nv_bfloat16* out, int32_t* status,
+                             long long wait_limit) {
   ArHeader* mine = reinterpret_cast<ArHeader*>(peers.base[rank]);
   __shared__ uint32_t s_epoch;
   __shared__ int s_ok;
@@ -119,57 +136,75 @@ __global__ void __launch_bounds__(kArThreads)
   }
   __syncthreads();
   const uint32_t e = s_epoch;
+  const int b = blockIdx.x;
+  const int64_t off = kArHeaderBytes + static_cast<int64_t>(e & 1u) * half_bytes;
+  const int64_t nvec = n / 8;
+  const int64_t lo = static_cast<int64_t>(b) * per_block;
+  const int64_t hi = lo + per_block < nvec ? lo + per_block : nvec;
+  const bool tail_block = (b == static_cast<int>(gridDim.x) - 1);
 
-  // 1. this rank's partial (written by the kernels before this one) is ready;
-  // every block announces it, so no block depends on another being resident
-  if (threadIdx.x < world) {
-    __threadfence_system();
-    ArHeader* peer = reinterpret_cast<ArHeader*>(peers.base[threadIdx.x]);
-    st_release_sys(&peer->start[rank], e);
-    if (!wait_reached(&mine->start[threadIdx.x], e)) s_ok = 0;
+  // 1. this rank's chunk into its own shared half (in may be out: each block
+  // reads its chunk of in here, before it writes the same chunk of out)
+  int4* own = reinterpret_cast<int4*>(peers.base[rank] + off);
+  for (int64_t i = lo + threadIdx.x; i < hi; i += kArThreads)
+    own[i] = reinterpret_cast<const int4*>(in)[i];
+  if (tail_block) {
+    unsigned short* own16 = reinterpret_cast<unsigned short*>(peers.base[rank] + off);
+    const unsigned short* in16 = reinterpret_cast<const unsigned short*>(in);
+    for (int64_t j = nvec * 8 + threadIdx.x; j < n; j += kArThreads) own16[j] = in16[j];
   }
   __syncthreads();
-  __threadfence_system();  // every thread's data loads come after the flags it waited on
+
+  // 2-3. publish chunk b of launch e to every rank; wait for every rank's
+  if (threadIdx.x < world) {
+    __threadfence_system();
+    st_release_sys(&reinterpret_cast<ArHeader*>(peers.base[threadIdx.x])->flag[rank][b], e);
+    if (!wait_reached(&mine->flag[threadIdx.x][b], e, wait_limit)) s_ok = 0;
+  }
+  __syncthreads();
   if (!s_ok && threadIdx.x == 0 && status) atomicOr(status, NVATTN_STATUS_TIMEOUT);
 
-  // 2. sum in rank order (fp32, from rank 0's value), one rounding to bf16
-  const int64_t nvec = n / 8;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kArThreads;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kArThreads + threadIdx.x; i < nvec;
-       i += stride) {
-    float acc[8];
-    load8(acc, ld_sys_v4(reinterpret_cast<const int4*>(peers.base[0] + kArHeaderBytes) + i));
-    for (int p = 1; p < world; ++p)
-      add8(acc, ld_sys_v4(reinterpret_cast<const int4*>(peers.base[p] + kArHeaderBytes) + i));
-    reinterpret_cast<int4*>(out)[i] = pack8(acc);
+  // 4. sum in rank order (fp32, from rank 0's value), one rounding to bf16;
+  // every rank's loads are issued before the adds
+  for (int64_t i0 = lo + threadIdx.x; i0 < hi; i0 += kArThreads * kArVecsPerThread) {
+    int4 v[kArVecsPerThread][kArMaxRanks];
+#pragma unroll
+    for (int u = 0; u < kArVecsPerThread; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * kArThreads;
+#pragma unroll
+      for (int p = 0; p < kArMaxRanks; ++p)
+        if (p < world && i < hi)
+          v[u][p] = ld_sys_v4(reinterpret_cast<const int4*>(peers.base[p] + off) + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kArVecsPerThread; ++u) {
+      const int64_t i = i0 + static_cast<int64_t>(u) * kArThreads;
+      if (i >= hi) break;
+      float acc[8];
+      load8(acc, v[u][0]);
+#pragma unroll
+      for (int p = 1; p < kArMaxRanks; ++p)
+        if (p < world) add8(acc, v[u][p]);
+      reinterpret_cast<int4*>(out)[i] = pack8(acc);
+    }
   }
-  if (blockIdx.x == 0) {
+  if (tail_block) {
     for (int64_t j = nvec * 8 + threadIdx.x; j < n; j += kArThreads) {
-      const unsigned short* d0 =
-          reinterpret_cast<const unsigned short*>(peers.base[0] + kArHeaderBytes);
-      float a = __uint_as_float(ld_sys_u16(d0 + j) << 16);
-      for (int p = 1; p < world; ++p) {
-        const unsigned short* dp =
-            reinterpret_cast<const unsigned short*>(peers.base[p] + kArHeaderBytes);
-        a += __uint_as_float(ld_sys_u16(dp + j) << 16);
-      }
+      float a = __uint_as_float(
+          ld_sys_u16(reinterpret_cast<const unsigned short*>(peers.base[0] + off) + j) << 16);
+      for (int p = 1; p < world; ++p)
+        a += __uint_as_float(
+            ld_sys_u16(reinterpret_cast<const unsigned short*>(peers.base[p] + off) + j) << 16);
       out[j] = __float2bfloat16_rn(a);
     }
   }
 
-  // 3. the last block of this rank: finished reading every partial of launch
-  // e; wait until every rank has, then record the launch
+  // the last block of this rank records launch e
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     const uint32_t prev = atomicAdd(&mine->done, 1u);
     if (prev == gridDim.x - 1) {
-      __threadfence_system();
-      for (int p = 0; p < world; ++p)
-        st_release_sys(&reinterpret_cast<ArHeader*>(peers.base[p])->end[rank], e);
-      bool ok = true;
-      for (int p = 0; p < world; ++p) ok = wait_reached(&mine->end[p], e) && ok;
-      if (!ok && status) atomicOr(status, NVATTN_STATUS_TIMEOUT);
       *reinterpret_cast<volatile uint32_t*>(&mine->done) = 0u;
       *reinterpret_cast<volatile uint32_t*>(&mine->epoch) = e;
       __threadfence();
@@ -189,9 +224,17 @@ static int ar_sms() {
 
 using namespace nvattn;
 
+static size_t ar_half_bytes(int64_t capacity_elems) {
+  return (static_cast<size_t>(capacity_elems) * 2 + 15) / 16 * 16;
+}
+
 extern "C" NVATTN_API size_t nvattn_ar_buffer_bytes(int64_t capacity_elems) {
   if (capacity_elems < 0) return 0;
-  return kArHeaderBytes + (static_cast<size_t>(capacity_elems) * 2 + 15) / 16 * 16;
+  return kArHeaderBytes + 2 * ar_half_bytes(capacity_elems);
+}
+
+extern "C" NVATTN_API int64_t nvattn_ar_set_wait_limit(int64_t cycles) {
+  return g_ar_wait_limit.exchange(cycles > 0 ? cycles : kWaitLimitCycles);
 }
 
 extern "C" NVATTN_API int nvattn_ar_alloc(size_t bytes, void** buffer, void* ipc_handle) {
@@ -241,14 +284,15 @@ extern "C" NVATTN_API int nvattn_ar_free(void* buffer) {
 }
 
 extern "C" NVATTN_API int nvattn_allreduce(const uint64_t* buffers, int32_t rank, int32_t world,
-                                           int64_t num_elems, int64_t capacity_elems, void* out,
-                                           int32_t* status, void* stream) {
+                                           int64_t num_elems, int64_t capacity_elems,
+                                           const void* in, void* out, int32_t* status,
+                                           void* stream) {
   clear_error();
   if (world < 1 || world > kArMaxRanks || rank < 0 || rank >= world)
     return fail(NVATTN_ERR_INVALID, "allreduce: world must be 1..8 and 0 <= rank < world");
   if (num_elems < 0 || num_elems > capacity_elems)
     return fail(NVATTN_ERR_INVALID, "allreduce: num_elems outside [0, capacity]");
-  if (!buffers || !out) return fail(NVATTN_ERR_INVALID, "allreduce: NULL buffers or out");
+  if (!buffers || !in || !out) return fail(NVATTN_ERR_INVALID, "allreduce: NULL buffers, in or out");
   ArPeers peers;
   for (int p = 0; p < kArMaxRanks; ++p) peers.base[p] = nullptr;
   for (int p = 0; p < world; ++p) {
@@ -256,19 +300,27 @@ extern "C" NVATTN_API int nvattn_allreduce(const uint64_t* buffers, int32_t rank
       return fail(NVATTN_ERR_INVALID, "allreduce: buffers must be non-NULL and 16-byte aligned");
     peers.base[p] = reinterpret_cast<char*>(buffers[p]);
   }
-  if (!aligned16(out)) return fail(NVATTN_ERR_INVALID, "allreduce: out must be 16-byte aligned");
+  if (!aligned16(in) || !aligned16(out))
+    return fail(NVATTN_ERR_INVALID, "allreduce: in and out must be 16-byte aligned");
   const uintptr_t own = static_cast<uintptr_t>(buffers[rank]);
+  const uintptr_t own_end = own + nvattn_ar_buffer_bytes(capacity_elems);
+  const uintptr_t bytes = static_cast<uintptr_t>(num_elems) * 2;
   const uintptr_t o = reinterpret_cast<uintptr_t>(out);
-  if (o + static_cast<uintptr_t>(num_elems) * 2 > own && o < own + nvattn_ar_buffer_bytes(capacity_elems))
-    return fail(NVATTN_ERR_INVALID, "allreduce: out overlaps the shared buffer");
+  const uintptr_t i = reinterpret_cast<uintptr_t>(in);
+  if ((o + bytes > own && o < own_end) || (i + bytes > own && i < own_end))
+    return fail(NVATTN_ERR_INVALID, "allreduce: in or out overlaps the shared buffer");
   if (num_elems == 0) return NVATTN_OK;
   const int64_t nvec = num_elems / 8;
-  int64_t grid = (nvec + kArThreads - 1) / kArThreads;
-  const int64_t cap = 2LL * ar_sms();
+  const int64_t per_launch = static_cast<int64_t>(kArThreads) * kArVecsPerThread;
+  int64_t grid = (nvec + per_launch - 1) / per_launch;
+  const int64_t cap = std::min<int64_t>(kArMaxBlocks, ar_sms());
   grid = grid < 1 ? 1 : (grid > cap ? cap : grid);
+  const int64_t per_block = (nvec + grid - 1) / grid;
   allreduce_oneshot_kernel<<<static_cast<unsigned>(grid), kArThreads, 0,
                              reinterpret_cast<cudaStream_t>(stream)>>>(
-      peers, rank, world, num_elems, static_cast<__nv_bfloat16*>(out), status);
+      peers, rank, world, num_elems, static_cast<int64_t>(ar_half_bytes(capacity_elems)),
+      per_block, static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), status,
+      g_ar_wait_limit.load());
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "allreduce_oneshot_kernel");
   return NVATTN_OK;

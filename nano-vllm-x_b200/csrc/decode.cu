@@ -417,6 +417,33 @@ int make_cache_map(CUtensorMap* map, const void* cache, int num_blocks, int bloc
   return make_tensor_map(map, cache, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Argument checks shared by both decode entry points (a negative batch is an
+// error; the caller handles batch == 0 before).
+static int check_decode_args(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                             const void* k_cache, const void* v_cache, const void* out,
+                             const int32_t* cache_seqlens, const int32_t* block_table,
+                             int64_t block_table_stride, int32_t max_blocks_per_seq,
+                             int32_t num_blocks, int32_t block_size, int32_t batch,
+                             int32_t num_heads, int32_t num_kv_heads, int32_t head_dim) {
+  if (batch < 0) return fail(NVATTN_ERR_INVALID, "paged_decode: negative batch");
+  if (!q || !k_cache || !v_cache || !out || !cache_seqlens || !block_table)
+    return fail(NVATTN_ERR_INVALID, "paged_decode: NULL pointer");
+  if (head_dim != kHeadDim) return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: head_dim must be 128");
+  if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads)
+    return fail(NVATTN_ERR_INVALID, "paged_decode: num_heads must be a multiple of num_kv_heads");
+  if (num_heads / num_kv_heads > kMaxGroup)
+    return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: more than 16 query heads per KV head");
+  if (block_size <= 0 || block_size % kTile)
+    return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: block_size must be a multiple of 64");
+  if (num_blocks <= 0 || max_blocks_per_seq <= 0 || block_table_stride < max_blocks_per_seq)
+    return fail(NVATTN_ERR_INVALID, "paged_decode: bad block table geometry");
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(NVATTN_ERR_INVALID, "paged_decode: caches must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_stride_tok & 1) || (q_stride_head & 1))
+    return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: q rows must be 4-byte aligned");
+  return NVATTN_OK;
+}
+
 }  // namespace nvattn
 
 using namespace nvattn;
@@ -442,24 +469,12 @@ extern "C" int nvattn_paged_decode(const void* q, int64_t q_stride_tok, int64_t 
                                    float softmax_scale, void* workspace, size_t workspace_bytes,
                                    int32_t* status, void* stream) {
   clear_error();
-  if (batch < 0) return fail(NVATTN_ERR_INVALID, "paged_decode: negative batch");
   if (batch == 0) return NVATTN_OK;
-  if (!q || !k_cache || !v_cache || !out || !cache_seqlens || !block_table)
-    return fail(NVATTN_ERR_INVALID, "paged_decode: NULL pointer");
-  if (head_dim != kHeadDim) return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: head_dim must be 128");
-  if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads)
-    return fail(NVATTN_ERR_INVALID, "paged_decode: num_heads must be a multiple of num_kv_heads");
+  int rc = check_decode_args(q, q_stride_tok, q_stride_head, k_cache, v_cache, out,
+                             cache_seqlens, block_table, block_table_stride, max_blocks_per_seq,
+                             num_blocks, block_size, batch, num_heads, num_kv_heads, head_dim);
+  if (rc) return rc;
   const int group = num_heads / num_kv_heads;
-  if (group > kMaxGroup)
-    return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: more than 16 query heads per KV head");
-  if (block_size <= 0 || block_size % kTile)
-    return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: block_size must be a multiple of 64");
-  if (num_blocks <= 0 || max_blocks_per_seq <= 0 || block_table_stride < max_blocks_per_seq)
-    return fail(NVATTN_ERR_INVALID, "paged_decode: bad block table geometry");
-  if (!aligned16(k_cache) || !aligned16(v_cache))
-    return fail(NVATTN_ERR_INVALID, "paged_decode: caches must be 16-byte aligned");
-  if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_stride_tok & 1) || (q_stride_head & 1))
-    return fail(NVATTN_ERR_UNSUPPORTED, "paged_decode: q rows must be 4-byte aligned");
 
   int nsplit, split_tiles;
   choose_split(batch, num_kv_heads, max_blocks_per_seq, block_size, &nsplit, &split_tiles);
@@ -471,7 +486,7 @@ extern "C" int nvattn_paged_decode(const void* q, int64_t q_stride_tok, int64_t 
     return fail(NVATTN_ERR_INVALID, "paged_decode: workspace must be 256-byte aligned");
 
   CUtensorMap kmap, vmap;
-  int rc = make_cache_map(&kmap, k_cache, num_blocks, block_size, num_kv_heads);
+  rc = make_cache_map(&kmap, k_cache, num_blocks, block_size, num_kv_heads);
   if (rc) return rc;
   rc = make_cache_map(&vmap, v_cache, num_blocks, block_size, num_kv_heads);
   if (rc) return rc;
@@ -577,6 +592,14 @@ extern "C" int nvattn_paged_decode_noalloc(
     int32_t* status, void* stream) {
   using namespace nvattn;
   clear_error();
+  if (batch == 0) return NVATTN_OK;
+  // The same argument checks as nvattn_paged_decode come first, so a bad call
+  // gets the same error from both entry points.
+  const int bad = check_decode_args(q, q_stride_tok, q_stride_head, k_cache, v_cache, out,
+                                    cache_seqlens, block_table, block_table_stride,
+                                    max_blocks_per_seq, num_blocks, block_size, batch, num_heads,
+                                    num_kv_heads, head_dim);
+  if (bad) return bad;
   const size_t need = nvattn_decode_workspace_bytes(batch, num_heads, num_kv_heads,
                                                     max_blocks_per_seq, block_size);
   if (need > kNoAllocScratchBytes) {

@@ -35,10 +35,17 @@ The engine is used unchanged except for what this environment lacks:
   (``nvattn.allreduce``, linear.py:152-155) for decode-sized messages;
   ``--attn reference`` keeps the engine's own flash-attn / Triton path.
 
-    python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz]
+    python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz] [--record]
+    python -m nvattn.e2e --compare reference.npz nvattn.npz
 
-Prints one JSON line: output tokens, seconds, tok/s. Needs the reference
-package importable (e.g. ``pip install --no-deps --target baseline/_ref``).
+Prints one JSON line: output tokens, seconds, tok/s. With ``--record`` rank 0
+also keeps, for every generated token, the top-2 logits (values and ids) of
+the row it was picked from; ``--out`` saves them beside the token ids.
+``--compare`` reads two such files (the first is the reference arm) and gives,
+per request, whether the ids are identical, the first divergent step, and the
+reference's top-1 minus top-2 logit margin at that step in bf16 ulps of its
+top logit. Needs the reference package importable (e.g. ``pip install
+--no-deps --target baseline/_ref``).
 """
 from __future__ import annotations
 
@@ -175,6 +182,26 @@ def patch_engine(attn: str) -> None:
             linear.RowParallelLinear.forward = _row_parallel_oneshot_forward
 
 
+class _RecordingSampler:
+    """Wraps rank 0's sampler: before sampling, keeps the top-2 logits of
+    every row that yields a token this step (a partial prefill chunk yields
+    none, scheduler.py postprocess), keyed by sequence id."""
+
+    def __init__(self, inner, runner):
+        self.inner = inner
+        self.runner = runner
+
+    def __call__(self, logits, temperatures):
+        top = logits.float().topk(2, dim=-1)
+        vals = top.values.cpu().numpy()
+        ids = top.indices.cpu().numpy()
+        for row, (seq_id, keep) in enumerate(self.runner._step_rows):
+            if keep:
+                self.runner._record.setdefault(seq_id, []).append(
+                    (vals[row, 0], vals[row, 1], ids[row, 0], ids[row, 1]))
+        return self.inner(logits, temperatures)
+
+
 def _runner_base():
     import nanovllm.engine.model_runner as model_runner
     return model_runner.ModelRunner
@@ -190,8 +217,17 @@ def _make_runner_class():
         def __init__(self, config, rank, event):
             self._attn = os.environ.get("NVATTN_E2E_ATTN", "nvattn")
             self._sample_step = 0
+            # top-2 logits per generated token, on rank 0 where the whole row
+            # is sampled (not in the fused arm at TP > 1: shards only)
+            self._recording = (os.environ.get("NVATTN_E2E_RECORD") == "1" and rank == 0 and
+                               not (self._attn == "nvattn-fused" and
+                                    config.tensor_parallel_size > 1))
+            self._record: dict[int, list] = {}
+            self._step_rows: list = []
             patch_engine(self._attn)
-            super().__init__(config, rank, event)
+            super().__init__(config, rank, event)  # workers (rank > 0) loop in here
+            if self._recording:
+                self.sampler = _RecordingSampler(self.sampler, self)
 
         def prepare_decode(self, seqs):
             """ModelRunner.prepare_decode (model_runner.py:172-188). In the
@@ -229,6 +265,23 @@ def _make_runner_class():
                         block_tables=gv["block_tables"][:B, :W])
             return gv["input_ids"][:B], gv["positions"][:B]
 
+        def exit(self):
+            """ModelRunner.exit (model_runner.py:40-49); with the one-shot
+            all-reduce, first gathers every rank's nvattn status word to rank 0
+            (all ranks run exit together, so the collective is matched)."""
+            if os.environ.get("NVATTN_E2E_ONESHOT_AR") == "1" and self.world_size > 1:
+                import torch.distributed as dist
+                from nvattn import ops
+                dev = torch.device("cuda", torch.cuda.current_device())
+                st = ops.status_tensor(dev).view(1)
+                every = torch.zeros(self.world_size, dtype=torch.int32, device=dev)
+                dist.all_gather_into_tensor(every, st)
+                bits = 0
+                for v in every.tolist():
+                    bits |= int(v)
+                self._final_status = bits
+            return super().exit()
+
         @torch.inference_mode()
         def run_model(self, input_ids, positions, is_prefill):
             """ModelRunner.run_model (model_runner.py:196-212); the graph's
@@ -244,6 +297,11 @@ def _make_runner_class():
             """ModelRunner.run (model_runner.py:214-220); in the fused arm at
             TP > 1 every rank samples its vocabulary shard and rank 0
             returns the merged tokens."""
+            if self._recording:
+                self._step_rows = [
+                    (seq.seq_id, not is_prefill or
+                     seq.num_cached_tokens + seq.num_scheduled_tokens == seq.num_tokens)
+                    for seq in seqs]
             if self._attn != "nvattn-fused" or self.world_size == 1:
                 return super().run(seqs, is_prefill)
             from nanovllm.utils.context import reset_context
@@ -283,9 +341,11 @@ def bench_workload(num_seqs: int = 256, max_input_len: int = 1024, max_output_le
 
 def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: int,
         enforce_eager: bool, model_dir: str | None = None, out: str | None = None,
-        oneshot_allreduce: bool = False) -> dict:
+        oneshot_allreduce: bool = False, record: bool = False,
+        max_num_seqs: int | None = None) -> dict:
     os.environ["NVATTN_E2E_ATTN"] = attn
     os.environ["NVATTN_E2E_ONESHOT_AR"] = "1" if oneshot_allreduce else "0"
+    os.environ["NVATTN_E2E_RECORD"] = "1" if record else "0"
     import nanovllm.engine.llm_engine as llm_engine  # noqa: F401  (reference)
     global E2EModelRunner
     E2EModelRunner = _make_runner_class()
@@ -298,10 +358,15 @@ def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: i
         model_dir = tmp.name
         write_model(Path(model_dir))
     prompts, max_tokens = bench_workload(num_seqs, max_input_len, max_output_len)
-    llm = LLM(model_dir, enforce_eager=enforce_eager, max_model_len=4096, tensor_parallel_size=tp)
+    extra = {} if max_num_seqs is None else {"max_num_seqs": max_num_seqs}
+    llm = LLM(model_dir, enforce_eager=enforce_eager, max_model_len=4096, tensor_parallel_size=tp,
+              **extra)
     sps = [SamplingParams(temperature=1.0, ignore_eos=True, max_tokens=m) for m in max_tokens]
     llm.generate([[1, 2, 3]], SamplingParams(max_tokens=4), use_tqdm=False)  # warm-up
     torch.cuda.synchronize()
+    runner = llm.model_runner
+    if getattr(runner, "_recording", False):
+        runner._record = {}
     t = time.time()
     outs = llm.generate(prompts, sps, use_tqdm=False)
     dt = time.time() - t
@@ -311,16 +376,90 @@ def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: i
            "unit": "tok/s", "enforce_eager": enforce_eager,
            "model": "random-init Qwen3-0.6B (28 layers, 16Q/8KV, d128, vocab 151936, bf16)",
            "decoding": "greedy", "oneshot_allreduce": oneshot_allreduce}
+    if max_num_seqs is not None:
+        res["max_num_seqs"] = max_num_seqs
+    arrays = {f"r{i}": np.array(o["token_ids"], np.int32) for i, o in enumerate(outs)}
+    if getattr(runner, "_recording", False):
+        # requests were added in order, so the i-th smallest sequence id is request i
+        for i, seq_id in enumerate(sorted(runner._record)):
+            arrays[f"m{i}"] = np.array(runner._record[seq_id], np.float32).reshape(-1, 4)
+        res["recorded"] = True
     if out:
-        np.savez_compressed(out, **{f"r{i}": np.array(o["token_ids"], np.int32)
-                                    for i, o in enumerate(outs)})
+        np.savez_compressed(out, **arrays)
     # Stop the engine's workers now (its atexit hook would do the same later).
     import atexit
     atexit.unregister(llm.exit)
     llm.exit()
+    if oneshot_allreduce and tp > 1:
+        # A flag wait of the peer-memory all-reduce that gave up (NVATTN_STATUS_TIMEOUT)
+        # means that launch summed partials a peer may not have finished writing: its
+        # tokens are not valid, and neither is the measurement. Every rank's status word
+        # was gathered to rank 0 when the engine exited.
+        st = getattr(runner, "_final_status", None)
+        res["status"] = st
+        if st:
+            raise RuntimeError(f"nvattn status word {st:#x} on some rank after generate "
+                               "(one-shot all-reduce wait timed out, or a bad slot or block): "
+                               "the run is invalid")
     if tmp is not None:
         tmp.cleanup()
     return res
+
+
+def _bf16_ulp(x: np.ndarray) -> np.ndarray:
+    """Spacing of bf16 numbers (8 significant bits) at |x|."""
+    ax = np.maximum(np.abs(x.astype(np.float64)), 2.0 ** -126)
+    return np.exp2(np.floor(np.log2(ax)) - 7)
+
+
+def compare(ref_path: str, ours_path: str, k_ulps: float = 4.0) -> dict:
+    """Per-request comparison of two ``--out`` files; the first is the
+    reference arm and must carry ``--record``'s top-2 logits.
+
+    For a request whose ids differ, the first divergent step s is the first
+    index where the two id lists differ. Up to s both arms saw the same
+    tokens, so at s they sampled from the same context; the reference's
+    margin there, (top1 - top2) / ulp(top1), says how close its own choice was
+    to a tie. Returns a summary with every request's record."""
+    a, b = np.load(ref_path), np.load(ours_path)
+    n = len([key for key in a.files if key.startswith("r")])
+    rows, all_margins = [], []
+    for i in range(n):
+        ra, rb = a[f"r{i}"], b[f"r{i}"]
+        m = a[f"m{i}"] if f"m{i}" in a.files else None
+        if m is not None:
+            all_margins.append((m[:, 0] - m[:, 1]) / _bf16_ulp(m[:, 0]))
+        same = ra.shape == rb.shape and np.array_equal(ra, rb)
+        row = {"request": i, "tokens": int(len(ra)), "identical": bool(same)}
+        if not same:
+            length = min(len(ra), len(rb))
+            diff = np.nonzero(ra[:length] != rb[:length])[0]
+            s = int(diff[0]) if len(diff) else length
+            row["first_divergence"] = s
+            if m is not None and s < len(m):
+                row["ref_margin_ulps"] = float((m[s, 0] - m[s, 1]) / _bf16_ulp(m[s, 0]))
+                row["ref_top2_ids"] = [int(m[s, 2]), int(m[s, 3])]
+                row["ours_token"] = int(rb[s]) if s < len(rb) else None
+            mb = b[f"m{i}"] if f"m{i}" in b.files else None
+            if mb is not None and s < len(mb):
+                row["ours_margin_ulps"] = float((mb[s, 0] - mb[s, 1]) / _bf16_ulp(mb[s, 0]))
+        rows.append(row)
+    div = [r for r in rows if not r["identical"]]
+    margins = np.array([r["ref_margin_ulps"] for r in div if "ref_margin_ulps" in r])
+    allm = np.concatenate(all_margins) if all_margins else np.zeros(0)
+    summary = {"requests": n, "identical": n - len(div), "diverged": len(div),
+               "k_ulps": k_ulps,
+               "diverged_within_k": int((margins <= k_ulps).sum()),
+               "max_ref_margin_at_divergence_ulps": float(margins.max()) if len(margins) else None,
+               "median_first_divergence_frac": float(np.median(
+                   [r["first_divergence"] / max(1, r["tokens"]) for r in div])) if div else None,
+               "all_steps_margin_median_ulps": float(np.median(allm)) if len(allm) else None,
+               "all_steps_frac_within_k": float((allm <= k_ulps).mean()) if len(allm) else None,
+               "margin_histogram_at_divergence": {
+                   str(lo): int(((margins >= lo) & (margins < hi)).sum())
+                   for lo, hi in ((0, 1), (1, 2), (2, 4), (4, 8), (8, 16), (16, 1e9))},
+               "rows": rows}
+    return summary
 
 
 def main() -> None:
@@ -338,13 +477,29 @@ def main() -> None:
     ap.add_argument("--oneshot-allreduce", action="store_true",
                     help="fused arm at TP > 1: row-parallel all-reduce through nvattn's "
                          "peer-memory kernel instead of NCCL")
+    ap.add_argument("--record", action="store_true",
+                    help="keep the top-2 logits of every generated token (saved by --out)")
+    ap.add_argument("--max-num-seqs", type=int, default=None,
+                    help="engine's max_num_seqs (reference default 512)")
+    ap.add_argument("--compare", nargs=2, metavar=("REF_NPZ", "OURS_NPZ"),
+                    help="compare two --out files (the first from the reference arm)")
+    ap.add_argument("--k-ulps", type=float, default=4.0)
     args = ap.parse_args()
+    if args.compare:
+        summary = compare(*args.compare, k_ulps=args.k_ulps)
+        rows = summary.pop("rows")
+        print(json.dumps(summary))
+        for r in rows:
+            if not r["identical"]:
+                print(json.dumps(r))
+        return
     if args.write_model:
         Path(args.write_model).mkdir(parents=True, exist_ok=True)
         write_model(Path(args.write_model))
         return
     res = run(args.tp, args.attn, args.num_seqs, args.max_input_len, args.max_output_len,
-              args.enforce_eager, args.model_dir, args.out, args.oneshot_allreduce)
+              args.enforce_eager, args.model_dir, args.out, args.oneshot_allreduce, args.record,
+              args.max_num_seqs)
     print(json.dumps(res), flush=True)
 
 

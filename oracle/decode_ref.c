@@ -86,18 +86,26 @@ static void decode_pair(const uint16_t* q, const uint16_t* k_cache, const uint16
 /*
  * q: (B, H, D) bf16; k_cache, v_cache: (num_blocks, bs, KVH, D) bf16;
  * cache_seqlens: (B,); block_table: (B, W); out: (B, H, D) fp32.
- * Returns 0, or -1 for unsupported sizes (D != 128, H / KVH > 16) or a length
- * beyond its block table (W * bs keys).
+ * Returns 0, or -1 for unsupported sizes (D != 128, H / KVH > 16), a length
+ * beyond its block table (W * bs keys), or a block id that a sequence's keys
+ * use outside [0, num_blocks) (checked before any cache read).
  */
 int oracle_decode_attention(const uint16_t* q, const uint16_t* k_cache,
                             const uint16_t* v_cache, const int32_t* cache_seqlens,
                             const int32_t* block_table, int64_t B, int64_t H, int64_t KVH,
-                            int64_t D, int64_t bs, int64_t W, float scale, float* out,
-                            int threads) {
+                            int64_t D, int64_t bs, int64_t W, int64_t num_blocks, float scale,
+                            float* out, int threads) {
   if (B < 0 || KVH <= 0 || H % KVH != 0 || H / KVH > 16 || D != kD || bs <= 0) return -1;
   const int64_t G = H / KVH;
-  for (int64_t b = 0; b < B; ++b)  /* every key must lie inside the sequence's block table */
+  for (int64_t b = 0; b < B; ++b) {
+    /* every key must lie inside the sequence's block table, in a real block */
     if (cache_seqlens[b] > W * bs) return -1;
+    const int64_t used = cache_seqlens[b] > 0 ? (cache_seqlens[b] + bs - 1) / bs : 0;
+    for (int64_t i = 0; i < used; ++i) {
+      const int32_t id = block_table[b * W + i];
+      if (id < 0 || id >= num_blocks) return -1;
+    }
+  }
   int failed = 0;
 #pragma omp parallel for schedule(dynamic, 1) num_threads(threads > 0 ? threads : 1)
   for (int64_t job = 0; job < B * KVH; ++job) {

@@ -188,7 +188,7 @@ def decode_attention_c(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
         lib = ctypes.CDLL(str(Path(__file__).resolve().parent / "liboracle_decode.so"))
         f = lib.oracle_decode_attention
         f.restype = ctypes.c_int
-        f.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 6 + [ctypes.c_float,
+        f.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 7 + [ctypes.c_float,
                                                                       ctypes.c_void_p, ctypes.c_int]
         _C_DECODE = f
     B, H, D = q.shape
@@ -200,10 +200,11 @@ def decode_attention_c(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
     bt = np.ascontiguousarray(block_table, dtype=np.int32)
     out = torch.empty(B, H, D, dtype=torch.float32)
     rc = _C_DECODE(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), lens.ctypes.data, bt.ctypes.data,
-                   B, H, KVH, D, bs, bt.shape[1], scale, out.data_ptr(),
+                   B, H, KVH, D, bs, bt.shape[1], k_cache.shape[0], scale, out.data_ptr(),
                    threads or os.cpu_count() or 1)
     if rc != 0:
-        raise ValueError("oracle_decode_attention: unsupported sizes or a length past its table")
+        raise ValueError("oracle_decode_attention: unsupported sizes, a length past its table "
+                         "or a block id outside the cache")
     return out
 
 

@@ -40,22 +40,33 @@ def max_err(a: torch.Tensor, b: torch.Tensor) -> float:
     return (a.float().cpu() - b.float().cpu()).abs().max().item()
 
 
-# Attention-output tolerance: max-abs 1e-2 between the bf16 kernel output and
-# the fp32-accumulated reference, plus the output's own bf16 rounding
-# (half an ulp = 2^-8 of |ref| at worst). Rounding alone reaches 0.0078 for
-# |ref| in [2, 4); flash-attn's outputs on the committed golden cases differ
-# from the fp32 oracle by up to 0.0072 at |ref| = 2.49.
+# Attention-output tolerance: max-abs 1e-2 between the kernel output and the
+# fp32-accumulated reference, beyond the output's own final rounding to bf16:
+# |out - ref| <= 1e-2 + half a bf16 ulp of ref. The half ulp is 2^(e-8) for
+# |ref| in [2^e, 2^(e+1)): 0.0039 below 2, 0.0078 in [2, 4). Rows with one or
+# two visible keys reach |o| of 2-4 (o is then a mix of one or two N(0,1) V
+# rows), and there a kernel that feeds P to the tensor cores as bf16 (as
+# flash-attn does) differs from the fp32 reference by up to ~2^-9 |v| from P's
+# rounding plus the output's half ulp. Every check prints its margin.
 ATOL = 1e-2
-RTOL = 2.0 ** -8
+
+
+def half_ulp_bf16(x: torch.Tensor) -> torch.Tensor:
+    """Half the spacing of bf16 numbers at |x| (8 significant bits)."""
+    ax = x.abs().clamp_min(2.0 ** -126)
+    return torch.exp2(torch.floor(torch.log2(ax)) - 8)
 
 
 def excess(a: torch.Tensor, b: torch.Tensor) -> float:
-    """max(|a - b| - (ATOL + RTOL |b|)); <= 0 means within tolerance."""
+    """max(|a - b| - (ATOL + half_ulp(b))); <= 0 means within tolerance."""
     a = a.float().cpu()
     b = b.float().cpu()
-    return ((a - b).abs() - (ATOL + RTOL * b.abs())).max().item()
+    return ((a - b).abs() - (ATOL + half_ulp_bf16(b))).max().item()
 
 
 def assert_close(a: torch.Tensor, b: torch.Tensor, what: str = "") -> None:
+    err = max_err(a, b)
     ex = excess(a, b)
-    assert ex <= 0, f"{what}: max-abs error {max_err(a, b):.4g} exceeds 1e-2 + 2^-8|ref| by {ex:.3g}"
+    print(f"[max-abs] {what or 'attention output'}: {err:.3e} (bound 1e-2 + half ulp; "
+          f"margin {-ex:.3e})")
+    assert ex <= 0, f"{what}: max-abs error {err:.4g} exceeds 1e-2 + half a bf16 ulp by {ex:.3g}"

@@ -1,16 +1,19 @@
 """The one-shot all-reduce's flag protocol, emulated on the CPU.
 
-allreduce_oneshot_kernel (csrc/allreduce.cu) synchronises ranks through
-flags in each rank's shared buffer: announce the launch count e to every
-rank, wait until every rank announced e, sum the partials, count finished
-blocks, and let the last block announce "finished reading e", wait for
-every rank's end flag and record e. Here each rank is a sequence of launches
-whose blocks are Python threads running those steps on shared arrays, with
-random delays to shuffle the interleavings; between launches the rank's
-"GEMM" overwrites its partial (stream order: only after its previous launch
-has completed). Every launch's output must be the sum of that launch's
-partials. A planted mistake, the end barrier left out, must be caught: a
-fast rank then overwrites its partial while a slow peer still reads it.
+allreduce_oneshot_kernel (csrc/allreduce.cu) cuts the message into one chunk
+per block. In launch e, block b of every rank copies its chunk of the rank's
+input into half e % 2 of the rank's shared buffer, publishes e into
+flag[rank][b] of every rank, waits until flag[p][b] of its own buffer has
+reached e for every rank p, sums chunk b of half e % 2 over the ranks, and
+the last block to finish records e. There is no closing barrier: the two
+halves stand in for it.
+
+Here each rank is a sequence of launches whose blocks are Python threads
+running those steps on shared arrays, with random delays to shuffle the
+interleavings; a launch completes when all its blocks have (stream order).
+Every launch's output must be the sum of that launch's inputs. A planted
+mistake, one data half instead of two, must be caught: a fast rank then
+overwrites its chunk while a slow peer still reads the previous launch's.
 """
 from __future__ import annotations
 
@@ -22,13 +25,12 @@ import numpy as np
 
 
 class _Rank:
-    def __init__(self, n):
-        self.start = np.zeros(8, np.int64)
-        self.end = np.zeros(8, np.int64)
+    def __init__(self, world, blocks, n):
+        self.flag = np.zeros((world, blocks), np.int64)
         self.epoch = 0
         self.done = 0
         self.lock = threading.Lock()
-        self.data = np.zeros(n, np.int64)
+        self.data = np.zeros((2, n), np.int64)
 
 
 def _wait(cond, limit=30.0):
@@ -40,50 +42,53 @@ def _wait(cond, limit=30.0):
     return True
 
 
-def _run(world, blocks, launches, n, end_barrier=True, seed=0):
-    ranks = [_Rank(n) for _ in range(world)]
+def _run(world, blocks, launches, n, halves=2, seed=0):
+    ranks = [_Rank(world, blocks, n) for _ in range(world)]
     rng = random.Random(seed)
-    delays = [[rng.random() * 2e-4 for _ in range(launches)] for _ in range(world)]
+    # rank r waits up to (r + 1) ms before its sum and 50 us before a launch, so
+    # low ranks tend to run ahead of high ranks' reads
+    delays = [[rng.random() * 1e-3 * (r + 1) for _ in range(launches)] for r in range(world)]
     outputs = [[None] * launches for _ in range(world)]
     timeouts = []
+    per = (n + blocks - 1) // blocks
 
-    def partial(r, k):
+    def given(r, k):
         return np.arange(n, dtype=np.int64) * (k + 1) + 1000 * r
 
-    def block(r, b, k, out):
+    def block(r, b, k, x, out):
         me = ranks[r]
         e = me.epoch + 1
-        for p in range(world):                        # announce
-            ranks[p].start[r] = e
-        for p in range(world):                        # wait for every rank's announcement
-            if not _wait(lambda: ranks[r].start[p] >= e):
-                timeouts.append(("start", r, k))
+        h = e % halves
+        lo, hi = b * per, min(n, (b + 1) * per)
+        for i in range(lo, hi):                        # copy this rank's chunk in
+            me.data[h, i] = x[i]
+            time.sleep(0)
+        for p in range(world):                         # publish chunk b of launch e
+            ranks[p].flag[r, b] = e
+        for p in range(world):                         # every rank's chunk b is in
+            if not _wait(lambda: ranks[r].flag[p, b] >= e):
+                timeouts.append((r, b, k))
         time.sleep(delays[r][k] * rng.random())
-        for i in range(b, n, blocks):                 # this block's slice, rank order
+        for i in range(lo, hi):                        # sum in rank order
             acc = 0
             for p in range(world):
-                acc += int(ranks[p].data[i])
+                acc += int(ranks[p].data[h, i])
                 time.sleep(0)
             out[i] = acc
-        with me.lock:                                 # count finished blocks
+        with me.lock:                                  # the last block records e
             prev = me.done
             me.done += 1
-        if prev == blocks - 1:                        # the last block
-            if end_barrier:
-                for p in range(world):
-                    ranks[p].end[r] = e
-                for p in range(world):
-                    if not _wait(lambda: ranks[r].end[p] >= e):
-                        timeouts.append(("end", r, k))
-            me.done = 0
-            me.epoch = e
+            if prev == blocks - 1:
+                me.done = 0
+                me.epoch = e
 
     def stream(r):
         for k in range(launches):
-            ranks[r].data[:] = partial(r, k)           # the GEMM before the launch
-            time.sleep(delays[r][k])
+            x = given(r, k)                            # the launch's input
+            time.sleep(delays[r][k] * 0.05)
             out = np.zeros(n, np.int64)
-            threads = [threading.Thread(target=block, args=(r, b, k, out)) for b in range(blocks)]
+            threads = [threading.Thread(target=block, args=(r, b, k, x, out))
+                       for b in range(blocks)]
             for t in threads:
                 t.start()
             for t in threads:
@@ -95,22 +100,22 @@ def _run(world, blocks, launches, n, end_barrier=True, seed=0):
         t.start()
     for t in streams:
         t.join()
-    want = [sum(partial(r, k) for r in range(world)) for k in range(launches)]
+    want = [sum(given(r, k) for r in range(world)) for k in range(launches)]
     correct = all(np.array_equal(outputs[r][k], want[k])
                   for r in range(world) for k in range(launches))
     return correct, timeouts
 
 
 def test_protocol_gives_every_launch_its_own_sum():
-    for world, blocks, seed in ((2, 3, 0), (3, 2, 1), (4, 3, 2)):
+    for world, blocks, seed in ((2, 3, 0), (3, 2, 1), (4, 3, 2), (2, 1, 3)):
         ok, timeouts = _run(world, blocks, launches=12, n=24, seed=seed)
         assert ok and not timeouts, (world, blocks, timeouts)
 
 
-def test_protocol_without_the_end_barrier_is_caught():
+def test_protocol_with_one_data_half_is_caught():
     caught = False
-    for seed in range(6):
-        ok, _ = _run(2, 2, launches=12, n=24, end_barrier=False, seed=seed)
+    for seed in range(8):
+        ok, _ = _run(2, 2, launches=12, n=24, halves=1, seed=seed)
         caught = caught or not ok
         if caught:
             break

@@ -1,5 +1,5 @@
-"""Paged split-K decode on the GPU against the oracle (max-abs 1e-2 plus the bf16
-output rounding, see helpers.ATOL/RTOL)."""
+"""Paged split-K decode on the GPU against the oracle (max-abs 1e-2 beyond the
+bf16 output rounding, helpers.ATOL)."""
 from __future__ import annotations
 
 import numpy as np

@@ -1,5 +1,5 @@
 """Varlen causal prefill (dense and paged/prefix-cache) on the GPU against
-the oracle (max-abs 1e-2 plus the bf16 output rounding, helpers.ATOL/RTOL)."""
+the oracle (max-abs 1e-2 beyond the bf16 output rounding, helpers.ATOL)."""
 from __future__ import annotations
 
 import numpy as np

@@ -97,16 +97,26 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     # one-shot all-reduce: argument checks before any launch
     import ctypes as C
     bufs = (C.c_uint64 * 2)(0x10000, 0x20000)
-    assert lib.nvattn_ar_buffer_bytes(1000) == 4096 + 2000
-    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 0, 8, 8, fake, None, None) == _lib.ERR_INVALID
-    assert lib.nvattn_allreduce(C.addressof(bufs), 2, 2, 8, 8, fake, None, None) == _lib.ERR_INVALID
-    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 9, 8, 8, fake, None, None) == _lib.ERR_INVALID
-    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 9, 8, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_ar_buffer_bytes(1000) == 4096 + 2 * 2000     # header + two halves
+    x = C.c_void_p(0x40000)
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 0, 8, 8, x, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 2, 2, 8, 8, x, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 9, 8, 8, x, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 9, 8, x, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 8, 8, None, fake, None,
+                                None) == _lib.ERR_INVALID            # no input
     bad = (C.c_uint64 * 2)(0x10000, 0x20008)
-    assert lib.nvattn_allreduce(C.addressof(bad), 0, 2, 8, 8, fake, None, None) == _lib.ERR_INVALID
-    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 8, 8, C.c_void_p(0x10000 + 4096), None,
+    assert lib.nvattn_allreduce(C.addressof(bad), 0, 2, 8, 8, x, fake, None, None) == _lib.ERR_INVALID
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 8, 8, x, C.c_void_p(0x10000 + 4096), None,
                                 None) == _lib.ERR_INVALID            # out inside the shared buffer
     assert b"overlaps" in lib.nvattn_last_error()
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 8, 8, C.c_void_p(0x10000 + 4096 + 16), fake,
+                                None, None) == _lib.ERR_INVALID      # in inside the shared buffer
+    assert lib.nvattn_allreduce(C.addressof(bufs), 0, 2, 8, 8, C.c_void_p(0x40008), fake, None,
+                                None) == _lib.ERR_INVALID            # misaligned input
+    prev = lib.nvattn_ar_set_wait_limit(1000)
+    assert prev == 2_000_000_000 and lib.nvattn_ar_set_wait_limit(0) == 1000
+    assert lib.nvattn_ar_set_wait_limit(0) == 2_000_000_000         # 0 restored the default
     assert lib.nvattn_ar_alloc(10, None, None) == _lib.ERR_INVALID
     assert lib.nvattn_ar_open(None, None) == _lib.ERR_INVALID
     assert lib.nvattn_ar_close(None) == _lib.OK and lib.nvattn_ar_free(None) == _lib.OK
@@ -127,6 +137,32 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
                                      None, None, 0, None, None) == _lib.ERR_INVALID  # misaligned
     assert lib.nvattn_decode_prepare(None, None, 0, 0, 256, 0, None, None, None, None, None, 0,
                                      None, None) == _lib.OK
+
+
+def test_noalloc_decode_checks_arguments_before_its_scratch_size():
+    """A bad call gets the error nvattn_paged_decode would give, not the
+    scratch-size error, even when the batch would also overflow the scratch."""
+    lib = _lib.load()
+    fake = ctypes.c_void_p(0x1000)
+
+    def noalloc(num_heads, num_kv_heads, block_size, head_dim=128, batch=128, width=128):
+        return lib.nvattn_paged_decode_noalloc(fake, 8192, 128, fake, fake, fake, 8192, 128, fake,
+                                               fake, width, width, 4096, block_size, batch,
+                                               num_heads, num_kv_heads, head_dim,
+                                               ctypes.c_float(0.1), None, None)
+
+    assert noalloc(64, 2, 256) == _lib.ERR_UNSUPPORTED  # 32 query heads per KV head
+    assert b"16 query heads" in lib.nvattn_last_error()
+    assert noalloc(60, 8, 256) == _lib.ERR_INVALID  # heads not a multiple of KV heads
+    assert b"multiple of num_kv_heads" in lib.nvattn_last_error()
+    assert noalloc(64, 8, 100) == _lib.ERR_UNSUPPORTED
+    assert b"block_size" in lib.nvattn_last_error()
+    assert noalloc(64, 8, 256, head_dim=64) == _lib.ERR_UNSUPPORTED
+    assert b"head_dim" in lib.nvattn_last_error()
+    assert noalloc(64, 8, 256, batch=-1) == _lib.ERR_INVALID
+    assert lib.nvattn_paged_decode_noalloc(None, 0, 0, None, None, None, 0, 0, None, None, 0, 0,
+                                           0, 256, 0, 64, 8, 128, ctypes.c_float(0.1), None,
+                                           None) == _lib.OK  # empty batch: nothing to do
 
 
 def test_python_wrapper_raises_through_error_path():
@@ -231,3 +267,24 @@ def test_package_surface():
         assert hasattr(nvattn, name)
     a = nvattn.Attention(16, 128, 128 ** -0.5, 8)
     assert a.k_cache.numel() == 0 and hasattr(a, "v_cache")
+
+
+def test_e2e_compare_finds_first_divergence_and_reference_margin(tmp_path):
+    """nvattn.e2e.compare on two hand-made --out files."""
+    from nvattn.e2e import compare
+    ref = {"r0": np.array([5, 6, 7], np.int32), "r1": np.array([1, 2, 3, 4], np.int32),
+           # top1, top2, id1, id2 per generated token (bf16 values)
+           "m0": np.array([[2.0, 1.0, 5, 9], [3.0, 2.0, 6, 9], [1.0, 0.5, 7, 9]], np.float32),
+           "m1": np.array([[4.0, 1.0, 1, 0], [4.0, 1.0, 2, 0], [2.0, 1.984375, 3, 8],
+                           [4.0, 1.0, 4, 0]], np.float32)}
+    ours = {"r0": ref["r0"].copy(), "r1": np.array([1, 2, 8, 0], np.int32)}
+    np.savez(tmp_path / "a.npz", **ref)
+    np.savez(tmp_path / "b.npz", **ours)
+    res = compare(str(tmp_path / "a.npz"), str(tmp_path / "b.npz"), k_ulps=4)
+    assert res["identical"] == 1 and res["diverged"] == 1
+    row = res["rows"][1]
+    assert row["first_divergence"] == 2 and row["ref_top2_ids"] == [3, 8]
+    assert row["ours_token"] == 8
+    # 2.0 - 1.984375 = 2^-6 = 1 ulp of 2.0 in bf16 (8 significant bits)
+    assert row["ref_margin_ulps"] == 1.0
+    assert res["diverged_within_k"] == 1

@@ -65,14 +65,16 @@ def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row():
     torch.cuda.synchronize()
     for out, ref_entry, q, kc, vc, lens, bt in outs:
         assert torch.isfinite(out.float()).all()
-        assert_close(out, ref_entry.float())
+        # the same kernels with the same split: only the workspace address
+        # differs, so the outputs must be equal bit for bit
+        assert torch.equal(out, ref_entry)
         ref = R.decode_attention(q, kc, vc, lens.numpy(), bt.numpy(), 128 ** -0.5)
-        assert_close(out, ref)
+        assert_close(out, ref, "no-alloc decode vs oracle")
     assert ops.read_status() == 0
 
 
 def test_noalloc_rejects_batches_beyond_its_scratch():
-    # configs[3] at TP1 needs ~68 MB of partials: more than the fixed 16 MiB
+    # configs[3] at TP1 needs ~34 MB of partials: more than the fixed 16 MiB
     B, H, KVH, width = 128, 64, 8, 128
     assert ops.decode_workspace_bytes(B, H, KVH, width, 256) > SCRATCH_BYTES
     q = torch.zeros(B, H, 128, dtype=torch.bfloat16, device=dev)
