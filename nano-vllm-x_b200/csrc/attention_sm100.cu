@@ -446,6 +446,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // Tiles where no row of the warp is masked take the lean path.
       const bool wfull = __all_sync(0xffffffffu, full_row);
+      // The last paged tile may hold stale rows whose V this warpgroup zeroes:
+      // that tile always takes the two passes below.
+      const bool zero_v_tile = MODE != kDense && j == ntiles - 1 && kend - j0 < kBN;
+      // Single pass (prefill modes): on a lean tile after the row's first,
+      // the exponentials are taken against the current reference max while
+      // the tile's max is found, with P kept in registers until the max is
+      // known. If no row of the warp grew its max by more than the rescale
+      // threshold (the usual case once a row has seen a few tiles), those P
+      // are exactly what the two passes below compute (same FMA, same exp2
+      // split) and they are stored; otherwise the warp redoes the tile in the
+      // two passes, from S, which nothing has overwritten yet. Tree mode
+      // keeps the two passes: it hands the first 64 keys of P to the MMA warp
+      // before the second 64 are computed, which a deferred store would undo.
+      if (!kSplitP && wfull && !zero_v_tile &&
+          __all_sync(0xffffffffu, m_used != -INFINITY || !valid)) {
+        const float base1 = (m_used == -INFINITY) ? 0.f : m_used;  // rows past the sequence
+        const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
+        const uint64_t nbase2 = pack_f32x2(-base1, -base1);
+        uint64_t sum2[2] = {pack_f32x2(0.f, 0.f), pack_f32x2(0.f, 0.f)};
+        float mx2[2] = {-INFINITY, -INFINITY};
+        uint32_t pk[64];
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          uint32_t sr[32];
+          sm100::tmem_ld32(t_lane + col_s(wg) + qq * 32, sr);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int ee = qq * 16 + e;  // pair index in the tile, 0..63
+            const uint64_t x2 = fma_f32x2((static_cast<uint64_t>(sr[2 * e + 1]) << 32) | sr[2 * e],
+                                          scale2, nbase2);
+            const float2 xx = unpack_f32x2(x2);
+            mx2[e & 1] = fmax3(mx2[e & 1], xx.x, xx.y);
+            const uint64_t p2 = ((ee & 31) % kPolyEvery == kPolyEvery - 1) ? exp2_poly_f32x2(x2)
+                                                                           : exp2_mufu_f32x2(x2);
+            sum2[e & 1] = add_f32x2(sum2[e & 1], p2);
+            const float2 pp = unpack_f32x2(p2);
+            pk[ee] = pack_bf16x2(pp.x, pp.y);
+          }
+        }
+        const float grow = fmaxf(mx2[0], mx2[1]);
+        if (!__any_sync(0xffffffffu, valid && grow > kRescaleThreshold)) {
+          sm100::tmem_st32(t_lane + col_s(wg), pk);
+          sm100::tmem_st32(t_lane + col_s(wg) + 32, pk + 32);
+          const float2 sm = unpack_f32x2(add_f32x2(sum2[0], sum2[1]));
+          l += sm.x + sm.y;
+          sm100::tmem_wait_st();
+          sm100::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->p_full[wg]);
+          continue;
+        }
+      }
       // Pass 1: row max of the raw scores, 64 columns per TMEM round trip,
       // in four independent chains (a single chain is 64 dependent maxes).
       float mr4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};

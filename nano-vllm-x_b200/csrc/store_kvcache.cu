@@ -2,11 +2,17 @@
 // nanovllm/layers/attention.py:10-40) and grouped in-cache slot moves.
 //
 // The reference runs one Triton program per token that loads D elements of K
-// and V and stores them at slot*D. Here one warp owns one token: its 32 lanes
-// move the K row then the V row in VEC-byte vectors (16 bytes when every
-// pointer, stride and D allow it), so each warp instruction touches 512
-// contiguous bytes on both the load and the store side. A CTA of 8 warps
-// covers 8 tokens; the grid is ceil(N/8) CTAs. Pure copy: bit-exact.
+// and V and stores them at slot*D. Here two layouts of the same copy, both in
+// VEC-byte vectors (16 bytes when every pointer, stride and D allow it), so
+// each warp instruction touches 512 contiguous bytes on the load and on the
+// store side:
+//   * few tokens (a decode batch): each thread moves one vector of one
+//     token's K row and the same vector of its V row; a CTA of 128 threads
+//     covers 128/vpr whole tokens (vpr = vectors per row: 128 at 8 KV heads
+//     x 128 dims), so a batch of a few hundred tokens spreads over every SM;
+//   * many tokens (a prefill chunk): one warp per token, each lane with
+//     eight vectors in flight (four of K, four of V) before its stores.
+// Pure copy: bit-exact.
 #include "common.cuh"
 
 namespace nvattn {
@@ -30,46 +36,90 @@ struct VecType<2> {
   using T = short;
 };
 
-constexpr int kStoreWarps = 8;
+constexpr int kVecThreads = 128;   // per CTA, vector-per-thread layout
+constexpr int kRowWarps = 8;       // per CTA, warp-per-token layout
+// Up to this many tokens x vectors per row, the vector-per-thread layout:
+// at most ~2 CTAs of it per SM.
+constexpr int64_t kVecLayoutMaxVectors = 2LL * 148 * 2 * kVecThreads * 4;
 
 template <int VEC>
-__global__ void __launch_bounds__(kStoreWarps * 32)
-    store_kvcache_kernel(const char* __restrict__ key, int64_t key_stride_b,
-                         const char* __restrict__ value, int64_t value_stride_b,
-                         char* __restrict__ k_cache, char* __restrict__ v_cache,
-                         const int32_t* __restrict__ slot_mapping, int64_t n_tokens,
-                         int64_t row_bytes, int64_t num_slots, int32_t* status) {
+__global__ void __launch_bounds__(kVecThreads)
+    store_kvcache_vec_kernel(const char* __restrict__ key, int64_t key_stride_b,
+                             const char* __restrict__ value, int64_t value_stride_b,
+                             char* __restrict__ k_cache, char* __restrict__ v_cache,
+                             const int32_t* __restrict__ slot_mapping, int64_t n_tokens,
+                             int64_t row_bytes, int64_t num_slots, int vpr, int tokens_per_cta,
+                             int32_t* status) {
   using V = typename VecType<VEC>::T;
-  const int lane = threadIdx.x & 31;
-  const int64_t tok = static_cast<int64_t>(blockIdx.x) * kStoreWarps + (threadIdx.x >> 5);
+  const int t_in = static_cast<int>(threadIdx.x) / vpr;  // 0 when a row has >= 128 vectors
+  if (t_in >= tokens_per_cta) return;
+  const int64_t tok = static_cast<int64_t>(blockIdx.x) * tokens_per_cta + t_in;
   if (tok >= n_tokens) return;
-  const int64_t slot = slot_mapping[tok];
+  const int first = static_cast<int>(threadIdx.x) - t_in * vpr;
+  const V* ksrc = reinterpret_cast<const V*>(key + tok * key_stride_b);
+  const V* vsrc = reinterpret_cast<const V*>(value + tok * value_stride_b);
+  // The rows' loads do not depend on the slot: issue them with the slot load,
+  // so the two latencies overlap (a skipped token's loads are simply unused).
+  const int32_t slot32 = __ldg(slot_mapping + tok);
+  V k = __ldg(ksrc + first), v = __ldg(vsrc + first);
+  const int64_t slot = slot32;
   if (slot == -1) return;  // attention.py:23
   if (slot < 0 || slot >= num_slots) {
-    if (lane == 0) set_status(status, NVATTN_STATUS_BAD_SLOT);
+    if (first == 0) set_status(status, NVATTN_STATUS_BAD_SLOT);
     return;
   }
+  V* kdst = reinterpret_cast<V*>(k_cache + slot * row_bytes);
+  V* vdst = reinterpret_cast<V*>(v_cache + slot * row_bytes);
+  for (int i = first;;) {
+    kdst[i] = k;
+    vdst[i] = v;
+    i += kVecThreads;
+    if (i >= vpr) break;
+    k = __ldg(ksrc + i);
+    v = __ldg(vsrc + i);
+  }
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(kRowWarps * 32)
+    store_kvcache_rows_kernel(const char* __restrict__ key, int64_t key_stride_b,
+                              const char* __restrict__ value, int64_t value_stride_b,
+                              char* __restrict__ k_cache, char* __restrict__ v_cache,
+                              const int32_t* __restrict__ slot_mapping, int64_t n_tokens,
+                              int64_t row_bytes, int64_t num_slots, int32_t* status) {
+  using V = typename VecType<VEC>::T;
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = static_cast<int64_t>(blockIdx.x) * kRowWarps + (threadIdx.x >> 5);
+  if (tok >= n_tokens) return;
   const int64_t nvec = row_bytes / VEC;
   const V* ksrc = reinterpret_cast<const V*>(key + tok * key_stride_b);
   const V* vsrc = reinterpret_cast<const V*>(value + tok * value_stride_b);
-  V* kdst = reinterpret_cast<V*>(k_cache + slot * row_bytes);
-  V* vdst = reinterpret_cast<V*>(v_cache + slot * row_bytes);
-  // Issue all loads of this lane before its stores so the two rows' reads
-  // overlap in flight.
-  for (int64_t i = lane; i < nvec; i += 64) {
-    V k0 = __ldg(ksrc + i);
-    V v0 = __ldg(vsrc + i);
-    const bool two = i + 32 < nvec;
-    V k1, v1;
-    if (two) {
-      k1 = __ldg(ksrc + i + 32);
-      v1 = __ldg(vsrc + i + 32);
+  const int32_t slot32 = __ldg(slot_mapping + tok);
+  // All loads of this lane (and the slot's) before its stores, so both rows'
+  // reads and the slot overlap in flight.
+  for (int64_t i = lane; i < nvec; i += 128) {
+    V k[4], v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (i + 32 * u < nvec) {
+        k[u] = __ldg(ksrc + i + 32 * u);
+        v[u] = __ldg(vsrc + i + 32 * u);
+      }
     }
-    kdst[i] = k0;
-    vdst[i] = v0;
-    if (two) {
-      kdst[i + 32] = k1;
-      vdst[i + 32] = v1;
+    const int64_t slot = slot32;
+    if (slot == -1) return;  // attention.py:23
+    if (slot < 0 || slot >= num_slots) {
+      if (lane == 0 && i == lane) set_status(status, NVATTN_STATUS_BAD_SLOT);
+      return;
+    }
+    V* kdst = reinterpret_cast<V*>(k_cache + slot * row_bytes);
+    V* vdst = reinterpret_cast<V*>(v_cache + slot * row_bytes);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (i + 32 * u < nvec) {
+        kdst[i + 32 * u] = k[u];
+        vdst[i + 32 * u] = v[u];
+      }
     }
   }
 }
@@ -156,30 +206,41 @@ extern "C" int nvattn_store_kvcache(const void* key, int64_t key_stride, const v
            (reinterpret_cast<uintptr_t>(k_cache) % v == 0) &&
            (reinterpret_cast<uintptr_t>(v_cache) % v == 0);
   };
-  const int64_t blocks = (num_tokens + kStoreWarps - 1) / kStoreWarps;
-  if (blocks > 0x7fffffff) return fail(NVATTN_ERR_INVALID, "store_kvcache: too many tokens");
+  if (row_bytes > (static_cast<int64_t>(1) << 30))
+    return fail(NVATTN_ERR_UNSUPPORTED, "store_kvcache: rows over 1 GiB");
+  const int vec = fits(16) ? 16 : fits(8) ? 8 : fits(4) ? 4 : 2;
+  const int vpr = static_cast<int>(row_bytes / vec);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  dim3 grid(static_cast<unsigned>(blocks)), block(kStoreWarps * 32);
   const char* kp = static_cast<const char*>(key);
   const char* vp = static_cast<const char*>(value);
   char* kc = static_cast<char*>(k_cache);
   char* vc = static_cast<char*>(v_cache);
-  if (fits(16))
-    store_kvcache_kernel<16><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
-                                                    vc, slot_mapping, num_tokens, row_bytes,
-                                                    num_slots, status);
-  else if (fits(8))
-    store_kvcache_kernel<8><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
-                                                   vc, slot_mapping, num_tokens, row_bytes,
-                                                   num_slots, status);
-  else if (fits(4))
-    store_kvcache_kernel<4><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
-                                                   vc, slot_mapping, num_tokens, row_bytes,
-                                                   num_slots, status);
-  else
-    store_kvcache_kernel<2><<<grid, block, 0, s>>>(kp, key_stride * 2, vp, value_stride * 2, kc,
-                                                   vc, slot_mapping, num_tokens, row_bytes,
-                                                   num_slots, status);
+  const int64_t ks = key_stride * 2, vs = value_stride * 2;
+  if (num_tokens * vpr <= kVecLayoutMaxVectors) {
+    const int tpc = vpr >= kVecThreads ? 1 : kVecThreads / vpr;
+    const dim3 grid(static_cast<unsigned>((num_tokens + tpc - 1) / tpc)), block(kVecThreads);
+#define NVATTN_STORE_VEC(V_)                                                                   \
+  store_kvcache_vec_kernel<V_><<<grid, block, 0, s>>>(kp, ks, vp, vs, kc, vc, slot_mapping,    \
+                                                      num_tokens, row_bytes, num_slots, vpr, tpc, \
+                                                      status)
+    if (vec == 16) NVATTN_STORE_VEC(16);
+    else if (vec == 8) NVATTN_STORE_VEC(8);
+    else if (vec == 4) NVATTN_STORE_VEC(4);
+    else NVATTN_STORE_VEC(2);
+#undef NVATTN_STORE_VEC
+  } else {
+    const int64_t blocks = (num_tokens + kRowWarps - 1) / kRowWarps;
+    if (blocks > 0x7fffffff) return fail(NVATTN_ERR_INVALID, "store_kvcache: too many tokens");
+    const dim3 grid(static_cast<unsigned>(blocks)), block(kRowWarps * 32);
+#define NVATTN_STORE_ROWS(V_)                                                               \
+  store_kvcache_rows_kernel<V_><<<grid, block, 0, s>>>(kp, ks, vp, vs, kc, vc, slot_mapping, \
+                                                       num_tokens, row_bytes, num_slots, status)
+    if (vec == 16) NVATTN_STORE_ROWS(16);
+    else if (vec == 8) NVATTN_STORE_ROWS(8);
+    else if (vec == 4) NVATTN_STORE_ROWS(4);
+    else NVATTN_STORE_ROWS(2);
+#undef NVATTN_STORE_ROWS
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "store_kvcache launch");
   return NVATTN_OK;

@@ -109,3 +109,42 @@ def test_flash_attn_varlen_func_keyword_form():
                                    causal=True, block_table=None)
     ref = R.varlen_attention(q, k, v, c.numpy(), c.numpy(), 128 ** -0.5, True)
     assert_close(o, ref)
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_row_max_growing_in_a_late_tile(paged):
+    """Keys whose scores jump far above everything before them (x10 keys at
+    positions 300, 460 and 700: the second half of tile 2, the first and
+    second halves of tile 3 and 5) make every row's running max grow past the
+    rescale threshold after its first tiles; the single-pass softmax must redo
+    those halves and rescale what it already accumulated."""
+    g = torch.Generator().manual_seed(31)
+    H, KVH, L = 16, 8, 800
+    q = torch.randn(L, H, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(L, KVH, 128, generator=g)
+    v = torch.randn(L, KVH, 128, generator=g).to(torch.bfloat16)
+    k[[300, 460, 700]] *= 10
+    k = k.to(torch.bfloat16)
+    c = cu([L])
+    if paged:
+        nblocks, bt = paged_layout([L], 256, seed=31)
+        kc = torch.zeros(nblocks, 256, KVH, 128, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+        for t in range(L):
+            kc[bt[0, t // 256], t % 256] = k[t]
+            vc[bt[0, t // 256], t % 256] = v[t]
+        # the last 8 of the 800 queries: they see every key
+        qn = q[-8:]
+        out = ops.varlen_prefill(qn.to(dev), kc.to(dev), vc.to(dev), cu([8]).to(dev), c.to(dev),
+                                 8, L, softmax_scale=128 ** -0.5, causal=True,
+                                 block_table=bt.to(dev))
+        ref = R.varlen_attention(qn, kc, vc, cu([8]).numpy(), c.numpy(), 128 ** -0.5, True,
+                                 bt.numpy())
+    else:
+        out = ops.varlen_prefill(q.to(dev), k.to(dev), v.to(dev), c.to(dev), c.to(dev), L, L,
+                                 softmax_scale=128 ** -0.5, causal=False)
+        ref = R.varlen_attention(q, k, v, c.numpy(), c.numpy(), 128 ** -0.5, False)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert_close(out, ref, f"late max growth ({'paged' if paged else 'dense'})")
+    assert ops.read_status() == 0

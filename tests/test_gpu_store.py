@@ -34,7 +34,9 @@ def test_matches_reference_triton_golden():
 
 @pytest.mark.parametrize("N,KVH,H,frac_skip", [(1, 8, 16, 0.0), (7, 8, 16, 0.3),
                                                (1000, 8, 16, 0.1), (16384, 8, 16, 0.0),
-                                               (333, 3, 6, 0.2), (64, 1, 8, 0.5)])
+                                               (333, 3, 6, 0.2), (64, 1, 8, 0.5),
+                                               # rows of exactly 256 and of 512 16-byte vectors
+                                               (40, 16, 32, 0.1), (20, 32, 64, 0.0)])
 def test_random_slots_bit_exact(N, KVH, H, frac_skip):
     g = torch.Generator().manual_seed(N * 31 + KVH)
     nb, bs = (N + 255) // 256 + 3, 256
@@ -59,20 +61,23 @@ def test_random_slots_bit_exact(N, KVH, H, frac_skip):
     assert ops.read_status() == 0
 
 
-def test_unaligned_stride_takes_narrow_vectors():
+@pytest.mark.parametrize("N", [50, 3000])  # both layouts: vector per thread, warp per token
+def test_unaligned_stride_takes_narrow_vectors(N):
     # value row stride of D+1 elements: 2-byte aligned only
-    N, KVH = 50, 2
+    KVH = 2
     D = KVH * 128
     buf = torch.randn(N * (D + 1) + 1, device=dev).to(torch.bfloat16)
     v = buf[1:1 + N * (D + 1)].view(N, D + 1)[:, :D].view(N, KVH, 128)
     assert v.stride(0) == D + 1 and v.stride(1) == 128
     k = torch.randn(N, KVH, 128, device=dev).to(torch.bfloat16)
-    kc = torch.zeros(1, 256, KVH, 128, dtype=torch.bfloat16, device=dev)
+    nb = (N + 255) // 256
+    kc = torch.zeros(nb, 256, KVH, 128, dtype=torch.bfloat16, device=dev)
     vc = torch.zeros_like(kc)
-    slots = torch.arange(N, dtype=torch.int32, device=dev) * 3 % 256
+    slots = (torch.arange(N, dtype=torch.int64, device=dev) * 7 % (nb * 256)).to(torch.int32)
+    assert len(set(slots.tolist())) == N
     ops.store_kvcache(k, v, kc, vc, slots)
     torch.cuda.synchronize()
-    ek = np.zeros((1, 256, KVH, 128), np.uint16)
+    ek = np.zeros((nb, 256, KVH, 128), np.uint16)
     ev = np.zeros_like(ek)
     R.store_kvcache(bf16_bits(k), np.ascontiguousarray(bf16_bits(v)), ek, ev, slots.cpu().numpy())
     assert np.array_equal(bf16_bits(kc), ek) and np.array_equal(bf16_bits(vc), ev)
