@@ -375,6 +375,7 @@ def run_nvattn(args):
                 secondary["decode_prepare"] = {"error": f"{e!r}"[:200]}
         if rank == 0 and world == 1:
             secondary["flash_attn_decode_cfg4"] = bench_flash_attn_decode(dev, args, H, KVH)
+            secondary["decode_e2e_shape"] = bench_decode_e2e_shape(dev, args, hbm_peak)
 
     traffic = None
     prof = REPO / "profiles" / "paged_decode_cfg4.json"
@@ -1035,6 +1036,77 @@ def bench_decode_prepare(dev, args):
                         "512 rows x 16 blocks; synchronised each step"}
 
 
+def bench_decode_e2e_shape(dev, args, hbm_peak, batches=(16, 64, 256)):
+    """Paged decode at the e2e model's shape (Qwen3-0.6B: 16Q/8KV, d128, 256-token
+    blocks) for batches of 16/64/256 sequences with contexts U[100,2048]
+    (numpy seed = batch), physical blocks permuted; flash-attn's decode on the
+    same caches beside it. Device time per call, 10 calls per CUDA graph;
+    caches used in turn so that >= 200 MB is touched between two reads of one."""
+    from nvattn import ops
+    try:
+        from flash_attn import flash_attn_with_kvcache
+    except Exception:  # noqa: BLE001
+        flash_attn_with_kvcache = None
+    H, KVH = 16, 8
+    res = {"metric": "paged decode GB/s at the e2e shape", "unit": "GB/s",
+           "workload": "16Q/8KV, d128, ctx U[100,2048], permuted 256-token blocks",
+           "timing": "10 calls per CUDA graph, device time per call; several caches in turn"}
+    for B in batches:
+        rng = np.random.default_rng(B)
+        lens = rng.integers(100, 2049, size=B).astype(np.int32)
+        nblk = (lens + BS - 1) // BS
+        tot = int(nblk.sum())
+        perm = rng.permutation(tot).astype(np.int32)
+        bt = np.full((B, int(nblk.max())), -1, np.int32)
+        pos = 0
+        for b in range(B):
+            bt[b, :nblk[b]] = perm[pos:pos + nblk[b]]
+            pos += nblk[b]
+        nbytes = int(lens.astype(np.int64).sum()) * KVH * D * 4
+        g = torch.Generator(device=dev).manual_seed(B)
+        sets = []
+        for _ in range(max(1, min(4, int(200e6 // nbytes) + 1))):
+            kc = torch.randn(tot, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+            vc = torch.randn(tot, BS, KVH, D, generator=g, device=dev).to(torch.bfloat16)
+            sets.append((kc, vc))
+        q = torch.randn(B, H, D, generator=g, device=dev).to(torch.bfloat16)
+        ld, bd = torch.from_numpy(lens).to(dev), torch.from_numpy(bt).to(dev)
+        ws = torch.empty(max(1, ops.decode_workspace_bytes(B, H, KVH, bt.shape[1], BS)),
+                         dtype=torch.uint8, device=dev)
+        out = torch.empty(B, H, D, dtype=torch.bfloat16, device=dev)
+        turn = [0]
+
+        def nxt():
+            turn[0] = (turn[0] + 1) % len(sets)
+            return sets[turn[0]]
+
+        def nv():
+            kc, vc = nxt()
+            ops.paged_decode(q, kc, vc, ld, bd, softmax_scale=D ** -0.5, workspace=ws, out=out)
+
+        for _ in range(args.warmup):
+            nv()
+        ms = graph_timed(nv, args.steps, dev)
+        row = {"us": round(ms * 1e3, 2), "value": round(nbytes / ms / 1e6, 1),
+               "frac_of_measured_hbm": round(nbytes / ms / 1e6 / hbm_peak, 4), "kv_bytes": nbytes}
+        if flash_attn_with_kvcache is not None:
+            q4 = q.unsqueeze(1)
+
+            def fa():
+                kc, vc = nxt()
+                flash_attn_with_kvcache(q4, kc, vc, cache_seqlens=ld, block_table=bd,
+                                        softmax_scale=D ** -0.5, causal=True)
+
+            for _ in range(args.warmup):
+                fa()
+            ms_fa = graph_timed(fa, args.steps, dev)
+            row["flash_attn"] = {"us": round(ms_fa * 1e3, 2), "value": round(nbytes / ms_fa / 1e6, 1)}
+        res[f"batch_{B}"] = row
+        del sets
+        torch.cuda.empty_cache()
+    return res
+
+
 def bench_flash_attn_decode(dev, args, H, KVH):
     """The reference's own GPU decode call (flash-attn, attention.py:72-74) on the
     same workload, for comparison; reports why if it cannot run."""
@@ -1188,6 +1260,8 @@ def run_only(args):
         res = bench_decode_prepare(dev, args)
     elif args.only == "store":
         res = bench_store_kvcache(dev, args, hbm_peak)
+    elif args.only == "decode_small":
+        res = bench_decode_e2e_shape(dev, args, hbm_peak, batches=(args.batch,))
     elif args.only == "e2e":
         torch.cuda.empty_cache()
         res = bench_e2e(args, world) if rank == 0 else None
@@ -1215,7 +1289,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
     ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler", "layer", "prep",
-                                       "store", "e2e"),
+                                       "store", "e2e", "decode_small"),
                     default=None,
                     help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")

@@ -37,6 +37,15 @@ constexpr int kDecConsumerWarps = 4;
 constexpr int kDecThreads = (kDecConsumerWarps + 1) * 32;
 constexpr int kMaxGroup = 16;                  // query heads per KV head handled per CTA
 constexpr int kOPad = 132;                     // fp32 row pitch of the merge buffer
+// Split policy (see choose_split); overridable at build time for tuning sweeps.
+#ifndef NVATTN_DEC_MIN_SPLIT_TILES
+#define NVATTN_DEC_MIN_SPLIT_TILES 4
+#endif
+#ifndef NVATTN_DEC_SPLIT_CTAS_PER_SM
+#define NVATTN_DEC_SPLIT_CTAS_PER_SM 8
+#endif
+constexpr int kMinSplitTiles = NVATTN_DEC_MIN_SPLIT_TILES;
+constexpr int kSplitCtasPerSm = NVATTN_DEC_SPLIT_CTAS_PER_SM;
 
 struct DecodeParams {
   const __nv_bfloat16* q;
@@ -83,6 +92,9 @@ __global__ void __launch_bounds__(kDecThreads, 2)
     return;
   }
   const int ntiles = (tok_end - tok_begin + kTile - 1) / kTile;
+  // The combine kernel may be scheduled from now on (it waits for this grid's
+  // completion before it reads anything).
+  asm volatile("griddepcontrol.launch_dependents;");
 
   extern __shared__ uint8_t smem_raw[];
   // Swizzled TMA tiles need 1024-byte alignment.
@@ -331,6 +343,10 @@ __global__ void __launch_bounds__(kDecThreads, 2)
 // Merges the split-K partials of one (sequence, query head) per warp-group.
 __global__ void __launch_bounds__(128)
     decode_combine_kernel(const DecodeParams p) {
+  // Launched as a programmatic dependent of paged_decode_kernel: it may start
+  // while the last decode CTAs run; this waits until that grid has completed
+  // and its partials are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int h = blockIdx.x;
   const int b = blockIdx.y;
   const int d = threadIdx.x;
@@ -373,9 +389,9 @@ static void choose_split(int batch, int num_kv_heads, int max_blocks, int block_
   const int64_t max_tiles = (static_cast<int64_t>(max_blocks) * block_size + kTile - 1) / kTile;
   const int64_t pairs = static_cast<int64_t>(batch) * num_kv_heads;
   int st = 64;
-  while (st > 4) {
+  while (st > kMinSplitTiles) {
     const int64_t ns = (max_tiles + st - 1) / st;
-    if (pairs * ns >= 8LL * sms) break;
+    if (pairs * ns >= static_cast<int64_t>(kSplitCtasPerSm) * sms) break;
     st >>= 1;
   }
   *split_tiles = st;
@@ -532,8 +548,16 @@ extern "C" int nvattn_paged_decode(const void* q, int64_t q_stride_tok, int64_t 
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "paged_decode launch");
   if (nsplit > 1) {
-    decode_combine_kernel<<<dim3(num_heads, batch), 128, 0, s>>>(p);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_heads, batch);
+    cfg.blockDim = dim3(128);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, decode_combine_kernel, p);
     if (e != cudaSuccess) return cuda_fail(e, "decode_combine launch");
   }
   return NVATTN_OK;

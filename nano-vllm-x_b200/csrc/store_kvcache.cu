@@ -38,9 +38,35 @@ struct VecType<2> {
 
 constexpr int kVecThreads = 128;   // per CTA, vector-per-thread layout
 constexpr int kRowWarps = 8;       // per CTA, warp-per-token layout
-// Up to this many tokens x vectors per row, the vector-per-thread layout:
-// at most ~2 CTAs of it per SM.
-constexpr int64_t kVecLayoutMaxVectors = 2LL * 148 * 2 * kVecThreads * 4;
+// Up to this many tokens x vectors per row (1024 tokens at 8 KV heads x 128
+// dims), the vector-per-thread layout; beyond, the warp-per-token one (both
+// measured on B200 from 64 to 16,384 tokens).
+constexpr int64_t kVecLayoutMaxVectors = 131072;
+
+// The rows are read once and the cache rows written once, so neither goes
+// through L1 (no_allocate) and the stores are streaming (evict first in L2).
+template <typename V>
+__device__ __forceinline__ V ld_stream(const V* p) {
+  return __ldg(p);
+}
+template <>
+__device__ __forceinline__ int4 ld_stream<int4>(const int4* p) {
+  int4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+template <typename V>
+__device__ __forceinline__ void st_stream(V* p, const V& v) {
+  *p = v;
+}
+template <>
+__device__ __forceinline__ void st_stream<int4>(int4* p, const int4& v) {
+  asm volatile("st.global.cs.v4.s32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
 
 template <int VEC>
 __global__ void __launch_bounds__(kVecThreads)
@@ -61,7 +87,7 @@ __global__ void __launch_bounds__(kVecThreads)
   // The rows' loads do not depend on the slot: issue them with the slot load,
   // so the two latencies overlap (a skipped token's loads are simply unused).
   const int32_t slot32 = __ldg(slot_mapping + tok);
-  V k = __ldg(ksrc + first), v = __ldg(vsrc + first);
+  V k = ld_stream(ksrc + first), v = ld_stream(vsrc + first);
   const int64_t slot = slot32;
   if (slot == -1) return;  // attention.py:23
   if (slot < 0 || slot >= num_slots) {
@@ -71,12 +97,12 @@ __global__ void __launch_bounds__(kVecThreads)
   V* kdst = reinterpret_cast<V*>(k_cache + slot * row_bytes);
   V* vdst = reinterpret_cast<V*>(v_cache + slot * row_bytes);
   for (int i = first;;) {
-    kdst[i] = k;
-    vdst[i] = v;
+    st_stream(kdst + i, k);
+    st_stream(vdst + i, v);
     i += kVecThreads;
     if (i >= vpr) break;
-    k = __ldg(ksrc + i);
-    v = __ldg(vsrc + i);
+    k = ld_stream(ksrc + i);
+    v = ld_stream(vsrc + i);
   }
 }
 
@@ -102,8 +128,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       if (i + 32 * u < nvec) {
-        k[u] = __ldg(ksrc + i + 32 * u);
-        v[u] = __ldg(vsrc + i + 32 * u);
+        k[u] = ld_stream(ksrc + i + 32 * u);
+        v[u] = ld_stream(vsrc + i + 32 * u);
       }
     }
     const int64_t slot = slot32;
@@ -117,8 +143,8 @@ __global__ void __launch_bounds__(kRowWarps * 32)
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       if (i + 32 * u < nvec) {
-        kdst[i + 32 * u] = k[u];
-        vdst[i + 32 * u] = v[u];
+        st_stream(kdst + i + 32 * u, k[u]);
+        st_stream(vdst + i + 32 * u, v[u]);
       }
     }
   }
