@@ -93,6 +93,9 @@ struct Params {
   int32_t nsplit, split_tiles, num_heads;
   float* ws_o;    // [total_q][num_heads][nsplit][128]
   float2* ws_ml;  // [total_q][num_heads][nsplit]
+  // Tree mode: sequences in decreasing key count (written by
+  // tree_order_kernel), so CTAs are dispatched longest first; null = in order.
+  const int32_t* order;
 };
 
 struct Barriers {
@@ -124,7 +127,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                    const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const Params p) {
-  const int b = blockIdx.z;
+  if (MODE == kTree) {
+    // launched as a programmatic dependent of tree_order_kernel: nothing
+    // below may be read before that grid (and all earlier work) completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
+  const int b = (MODE == kTree && p.order != nullptr) ? p.order[blockIdx.z] : blockIdx.z;
   const int g = blockIdx.y;
   const int split = blockIdx.x % p.nsplit;
   const int m = gridDim.x / p.nsplit - 1 - blockIdx.x / p.nsplit;  // heaviest row blocks first
@@ -133,7 +141,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Tree mode hands P to the MMA warp in two 64-key halves, so the P V of the
   // first half overlaps the softmax of the second (measured: +4% on tree,
   // -2% on prefill, which keeps one hand-off).
-  constexpr bool kSplitP = MODE == kTree;
+#ifndef NVATTN_TREE_SPLIT_P
+#define NVATTN_TREE_SPLIT_P 1
+#endif
+  constexpr bool kSplitP = MODE == kTree && NVATTN_TREE_SPLIT_P;
 
   // ------------------------------------------------ sequence geometry
   const int q_begin = p.cu_q[b];
@@ -459,7 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // two passes, from S, which nothing has overwritten yet. Tree mode
       // keeps the two passes: it hands the first 64 keys of P to the MMA warp
       // before the second 64 are computed, which a deferred store would undo.
-      if (!kSplitP && wfull && !zero_v_tile &&
+#ifndef NVATTN_TREE_SINGLE_PASS
+#define NVATTN_TREE_SINGLE_PASS 0
+#endif
+      if (!kSplitP && (MODE != kTree || NVATTN_TREE_SINGLE_PASS) && wfull && !zero_v_tile &&
           __all_sync(0xffffffffu, m_used != -INFINITY || !valid)) {
         const float base1 = (m_used == -INFINITY) ? 0.f : m_used;  // rows past the sequence
         const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
@@ -712,6 +726,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Tree mode: the order in which sequences' CTAs are dispatched, longest
+// (most keys: context + draft) first, ties by index. With one wave or more of
+// CTAs and no key split, the hardware's in-order dispatch to free SMs then
+// schedules the items longest-processing-time first, which keeps the last SM
+// to finish close to the average.
+constexpr int kOrderMaxSeqs = 1024;
+
+__global__ void __launch_bounds__(kOrderMaxSeqs)
+    tree_order_kernel(const int32_t* __restrict__ ctx_lens, const int32_t* __restrict__ cu_q,
+                      int num_seqs, int32_t* __restrict__ order) {
+  __shared__ int32_t key[kOrderMaxSeqs];
+  for (int i = threadIdx.x; i < num_seqs; i += blockDim.x)
+    key[i] = max(0, ctx_lens[i]) + max(0, cu_q[i + 1] - cu_q[i]);
+  __syncthreads();
+  // Let the dependent attention grid launch now: it waits for this grid's
+  // completion before it reads the order.
+  asm volatile("griddepcontrol.launch_dependents;");
+  for (int i = threadIdx.x; i < num_seqs; i += blockDim.x) {
+    const int ki = key[i];
+    int rank = 0;
+    for (int j = 0; j < num_seqs; ++j) {
+      const int kj = key[j];
+      rank += (kj > ki) || (kj == ki && j < i);
+    }
+    order[rank] = i;
+  }
+}
+
 // Merges the split-K partials of the tree mode: one warp per (node, query
 // head); lane i owns dims 4i..4i+3. Splits past the sequence's keys were
 // never run and are not read.
@@ -816,8 +858,23 @@ int launch(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, 
   if (blocks_m <= 0) return NVATTN_OK;
   if (num_seqs > 65535) return fail(NVATTN_ERR_UNSUPPORTED, "more than 65535 sequences");
   dim3 grid(blocks_m * p.nsplit, p.num_kv_heads, num_seqs);
-  attn_tc_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (MODE == kTree && p.order != nullptr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, attn_tc_kernel<MODE>, qm, km, vm, p);
+  } else {
+    attn_tc_kernel<MODE><<<grid, kThreads, kSmemBytes, stream>>>(qm, km, vm, p);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return cuda_fail(e, "attn_tc_kernel launch");
   if (p.nsplit > 1) {
     const int per_seq = max_tokens * p.num_heads;
@@ -891,9 +948,13 @@ static void tree_split(int num_seqs, int num_heads, int num_kv_heads, int max_no
   const int64_t ctas = static_cast<int64_t>(num_seqs) * num_kv_heads * blocks_m;
   const int max_tiles = static_cast<int>(
       (static_cast<int64_t>(max_blocks) * block_size + tc::kBN - 1) / tc::kBN);
+  // One wave or more of items: no split (no partials to write and merge);
+  // the items are dispatched longest first instead (tree_order_kernel).
+  // Fewer: split each item's keys so that ~4 waves of CTAs fill the GPU.
   int ns = 1;
-  const int64_t target = 4LL * sm_count();
-  if (ctas < target) {
+  const int sms = sm_count();
+  if (ctas < sms) {
+    const int64_t target = 4LL * sms;
     ns = static_cast<int>((target + ctas - 1) / ctas);
     ns = std::min(ns, std::max(1, max_tiles / 8));
   }
@@ -901,11 +962,22 @@ static void tree_split(int num_seqs, int num_heads, int num_kv_heads, int max_no
   *split_tiles = (max_tiles + *nsplit - 1) / *nsplit;
 }
 
-static size_t tree_ws_bytes(int64_t total_q, int num_heads, int nsplit) {
-  if (nsplit <= 1) return 0;
-  const size_t n = static_cast<size_t>(total_q) * num_heads * nsplit;
-  const size_t o_bytes = (n * kHeadDim * sizeof(float) + 255) & ~static_cast<size_t>(255);
-  return o_bytes + n * sizeof(float2);
+// Tree workspace: the dispatch order (one int32 per sequence, when there are
+// at most kOrderMaxSeqs sequences), then with a key split the fp32 partial O
+// and the (max, sum) pairs; each region 256-byte aligned.
+static size_t tree_order_bytes(int num_seqs) {
+  return num_seqs <= tc::kOrderMaxSeqs ? (static_cast<size_t>(num_seqs) * 4 + 255) & ~size_t(255)
+                                       : 0;
+}
+
+static size_t tree_ws_bytes(int num_seqs, int64_t total_q, int num_heads, int nsplit) {
+  size_t bytes = tree_order_bytes(num_seqs);
+  if (nsplit > 1) {
+    const size_t n = static_cast<size_t>(total_q) * num_heads * nsplit;
+    const size_t o_bytes = (n * kHeadDim * sizeof(float) + 255) & ~static_cast<size_t>(255);
+    bytes += o_bytes + n * sizeof(float2);
+  }
+  return bytes;
 }
 
 }  // namespace nvattn
@@ -921,7 +993,7 @@ extern "C" size_t nvattn_tree_workspace_bytes(int32_t num_seqs, int32_t max_node
   int nsplit, split_tiles;
   tree_split(num_seqs, num_heads, num_kv_heads, max_nodes, max_blocks_per_seq, block_size, &nsplit,
              &split_tiles);
-  return tree_ws_bytes(total_q, num_heads, nsplit);
+  return tree_ws_bytes(num_seqs, total_q, num_heads, nsplit);
 }
 
 extern "C" int nvattn_varlen_prefill(
@@ -1029,18 +1101,30 @@ extern "C" int nvattn_tree_verify(const void* q, int64_t q_stride_tok, int64_t q
   p.causal = 1;
   tree_split(num_seqs, num_heads, num_kv_heads, max_nodes, max_blocks_per_seq, block_size,
              &p.nsplit, &p.split_tiles);
-  const size_t need = tree_ws_bytes(total_q, num_heads, p.nsplit);
+  const size_t need = tree_ws_bytes(num_seqs, total_q, num_heads, p.nsplit);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (need > 0) {
     if (workspace == nullptr || workspace_bytes < need)
       return fail(NVATTN_ERR_WORKSPACE,
                   "tree_verify: workspace smaller than nvattn_tree_workspace_bytes()");
     if (reinterpret_cast<uintptr_t>(workspace) & 255)
       return fail(NVATTN_ERR_INVALID, "tree_verify: workspace must be 256-byte aligned");
-    const size_t n = static_cast<size_t>(total_q) * num_heads * p.nsplit;
-    const size_t o_bytes = (n * kHeadDim * sizeof(float) + 255) & ~static_cast<size_t>(255);
-    p.ws_o = static_cast<float*>(workspace);
-    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) + o_bytes);
+    char* ws = static_cast<char*>(workspace);
+    const size_t ob = tree_order_bytes(num_seqs);
+    if (ob > 0) {
+      int32_t* order = reinterpret_cast<int32_t*>(ws);
+      tc::tree_order_kernel<<<1, tc::kOrderMaxSeqs, 0, s>>>(context_lens, cu_seqlens_q, num_seqs,
+                                                             order);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_fail(e, "tree_order_kernel launch");
+      p.order = order;
+    }
+    if (p.nsplit > 1) {
+      const size_t n = static_cast<size_t>(total_q) * num_heads * p.nsplit;
+      const size_t o_bytes = (n * kHeadDim * sizeof(float) + 255) & ~static_cast<size_t>(255);
+      p.ws_o = reinterpret_cast<float*>(ws + ob);
+      p.ws_ml = reinterpret_cast<float2*>(ws + ob + o_bytes);
+    }
   }
-  return tc::launch<tc::kTree>(qm, km, vm, p, num_seqs, max_nodes,
-                               reinterpret_cast<cudaStream_t>(stream));
+  return tc::launch<tc::kTree>(qm, km, vm, p, num_seqs, max_nodes, s);
 }
