@@ -618,10 +618,10 @@ def bench_store_kvcache(dev, args, hbm_peak):
             k, v = k.view(n, KVH, D), v.view(n, KVH, D)
             kc = torch.zeros(nb, BS, KVH, D, dtype=torch.bfloat16, device=dev)
             vc = torch.zeros_like(kc)
-            if n >= BS:
+            if name.startswith("prefill"):
                 blocks = torch.randperm(nb, generator=g, device=dev)[:(n + BS - 1) // BS]
                 slots = (blocks[:, None] * BS + torch.arange(BS, device=dev)[None]).flatten()[:n]
-            else:
+            else:  # decode: one new token per sequence, each in its own block
                 slots = torch.randperm(nb * BS, generator=g, device=dev)[:n]
             sets.append((qkv, k, v, kc, vc, slots.to(torch.int32)))
         nbytes = float(2 * n * KVH * D * 2 * 2 + 4 * n)

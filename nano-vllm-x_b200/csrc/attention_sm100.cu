@@ -141,10 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Tree mode hands P to the MMA warp in two 64-key halves, so the P V of the
   // first half overlaps the softmax of the second (measured: +4% on tree,
   // -2% on prefill, which keeps one hand-off).
-#ifndef NVATTN_TREE_SPLIT_P
-#define NVATTN_TREE_SPLIT_P 1
-#endif
-  constexpr bool kSplitP = MODE == kTree && NVATTN_TREE_SPLIT_P;
+  constexpr bool kSplitP = MODE == kTree;
 
   // ------------------------------------------------ sequence geometry
   const int q_begin = p.cu_q[b];
@@ -470,10 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // two passes, from S, which nothing has overwritten yet. Tree mode
       // keeps the two passes: it hands the first 64 keys of P to the MMA warp
       // before the second 64 are computed, which a deferred store would undo.
-#ifndef NVATTN_TREE_SINGLE_PASS
-#define NVATTN_TREE_SINGLE_PASS 0
-#endif
-      if (!kSplitP && (MODE != kTree || NVATTN_TREE_SINGLE_PASS) && wfull && !zero_v_tile &&
+      if (!kSplitP && wfull && !zero_v_tile &&
           __all_sync(0xffffffffu, m_used != -INFINITY || !valid)) {
         const float base1 = (m_used == -INFINITY) ? 0.f : m_used;  // rows past the sequence
         const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2);
