@@ -674,6 +674,27 @@ def bench_store_kvcache(dev, args, hbm_peak):
     return res
 
 
+# Variables torchrun sets for its workers. A process started from a worker
+# must not see them: with TORCHELASTIC_USE_AGENT_STORE set, every rank of a
+# new tcp:// process group (the reference engine's, model_runner.py:26)
+# connects as a client to a store nobody serves, and waits for the timeout.
+_LAUNCHER_VARS = ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK",
+                  "GROUP_WORLD_SIZE", "ROLE_RANK", "ROLE_WORLD_SIZE", "ROLE_NAME",
+                  "MASTER_ADDR", "MASTER_PORT")
+
+
+def engine_env(base) -> dict:
+    """The environment for an engine process started from a bench rank: no
+    launcher variables, and the package, repository and reference install on
+    PYTHONPATH."""
+    env = {k: v for k, v in base.items()
+           if k not in _LAUNCHER_VARS and not k.startswith("TORCHELASTIC_")}
+    env["PYTHONPATH"] = os.pathsep.join([str(REPO / "nano-vllm-x_b200"), str(REPO),
+                                         str(REPO / "baseline" / "_ref"),
+                                         env.get("PYTHONPATH", "")])
+    return env
+
+
 def bench_e2e(args, world):
     """configs[1] end to end (the third part of the metric; the reference's
     bench.py:8-28 workload through its own engine): nvattn.e2e runs the fused
@@ -686,13 +707,7 @@ def bench_e2e(args, world):
         import nanovllm  # noqa: F401
     except Exception as e:  # noqa: BLE001
         return {"unavailable": f"reference engine not importable: {e!r}"[:200]}
-    env = dict(os.environ)
-    for key in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK",
-                "ROLE_RANK", "MASTER_ADDR", "MASTER_PORT", "TORCHELASTIC_RUN_ID"):
-        env.pop(key, None)  # the engine sets up its own process group
-    env["PYTHONPATH"] = os.pathsep.join([str(REPO / "nano-vllm-x_b200"), str(REPO),
-                                         str(REPO / "baseline" / "_ref"),
-                                         env.get("PYTHONPATH", "")])
+    env = engine_env(os.environ)
     res = {"metric": "e2e out tok/s", "unit": "tok/s", "tp": world,
            "workload": "configs[1]: 256 requests (bench.py draw order, random.seed(0)), input and "
                        "output lengths U[100,1024], ignore_eos, greedy; random-init Qwen3-0.6B, "

@@ -111,3 +111,28 @@ def test_head_sharded_attention_equals_unsharded_world2():
     assert mx == 2.0 and sm == 3.0
     assert kshape == (2, 5)
     assert np.array_equal(toks, R.greedy_tokens(logits).numpy()) and toks[0] == 499
+
+
+def test_engine_env_lets_a_child_set_up_its_own_process_group():
+    """bench.py runs the end-to-end engine in a child of a torchrun rank. The
+    child's environment (bench.engine_env) must carry none of torchrun's
+    variables: with TORCHELASTIC_USE_AGENT_STORE inherited, a tcp:// process
+    group never finds its store and waits out its timeout."""
+    import subprocess
+    import sys
+
+    import bench
+    port = _free_port()
+    rank_env = dict(os.environ, RANK="0", LOCAL_RANK="0", WORLD_SIZE="2", MASTER_ADDR="127.0.0.1",
+                    MASTER_PORT=str(_free_port()), TORCHELASTIC_USE_AGENT_STORE="True",
+                    TORCHELASTIC_RESTART_COUNT="0", TORCHELASTIC_RUN_ID="x", GROUP_RANK="0")
+    env = bench.engine_env(rank_env)
+    assert not [k for k in env if k.startswith("TORCHELASTIC_")]
+    assert "RANK" not in env and "MASTER_PORT" not in env
+    assert str(REPO / "nano-vllm-x_b200") in env["PYTHONPATH"].split(os.pathsep)
+    probe = ("import datetime, torch.distributed as dist; "
+             f"dist.init_process_group('gloo', 'tcp://127.0.0.1:{port}', world_size=1, rank=0, "
+             "timeout=datetime.timedelta(seconds=20)); print('ok'); dist.destroy_process_group()")
+    r = subprocess.run([sys.executable, "-c", probe], env=env, capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stderr[-500:]

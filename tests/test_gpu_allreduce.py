@@ -56,7 +56,7 @@ def _worker(rank, world, port, paths, result_q):
         from nvattn.allreduce import OneShotAllReduce, row_parallel_forward
         from oracle import reference_math as R
         ops.read_status(dev)
-        cap = 512 * 1024
+        cap = 1024 * 1024
         ar = OneShotAllReduce(cap)
         checks = []
 
@@ -73,7 +73,7 @@ def _worker(rank, world, port, paths, result_q):
                 return torch.equal(ours, ref)
             return torch.allclose(ours.float(), ref.float(), atol=0.05, rtol=0.02)
 
-        for n in (1, 8, 1000, 4099, 256 * 1024, 300_001, cap):
+        for n in (1, 8, 1000, 4099, 256 * 1024, 300_001, cap):  # cap: 2 MB
             g = torch.Generator(device=dev).manual_seed(n * 10 + rank)
             mine = (torch.randn(n, generator=g, device=dev) * 4).to(torch.bfloat16)
             ref = mine.clone()
