@@ -695,6 +695,56 @@ def engine_env(base) -> dict:
     return env
 
 
+def bench_store_sweep(dev, args):
+    """The scatter at 64..16,384 tokens (one random slot each) beside the
+    reference's Triton kernel: device time per call, 10 calls per CUDA graph,
+    4 input sets and caches in turn."""
+    from nvattn import ops
+    reference_on_path()
+    try:
+        from nanovllm.layers.attention import store_kvcache as ref_store
+    except Exception:  # noqa: BLE001
+        ref_store = None
+    H, KVH = 16, 8
+    g = torch.Generator(device=dev).manual_seed(1)
+    res = {"metric": "store_kvcache us per call", "unit": "us", "higher_is_better": False}
+    for n in (64, 256, 1024, 2048, 4096, 16384):
+        nb = max(64, (n + BS - 1) // BS * 2)
+        sets = []
+        for _ in range(4):
+            qkv = torch.randn(n, (H + 2 * KVH) * D, generator=g, device=dev).to(torch.bfloat16)
+            _, k, v = qkv.split([H * D, KVH * D, KVH * D], dim=-1)
+            kc = torch.zeros(nb, BS, KVH, D, dtype=torch.bfloat16, device=dev)
+            sl = torch.randperm(nb * BS, generator=g, device=dev)[:n].to(torch.int32)
+            sets.append((k.view(n, KVH, D), v.view(n, KVH, D), kc, torch.zeros_like(kc), sl))
+        turn = [0]
+
+        def nxt():
+            turn[0] = (turn[0] + 1) % len(sets)
+            return sets[turn[0]]
+
+        def nv():
+            k, v, kc, vc, sl = nxt()
+            ops.store_kvcache(k, v, kc, vc, sl)
+
+        def rf():
+            k, v, kc, vc, sl = nxt()
+            ref_store(k, v, kc, vc, sl)
+
+        # both implementations warmed up (the Triton kernel compiled) before either is timed
+        for _ in range(max(args.warmup, 3)):
+            nv()
+            if ref_store is not None:
+                rf()
+        row = {"nvattn": round(graph_timed(nv, args.steps, dev) * 1e3, 2)}
+        if ref_store is not None:
+            row["reference_triton"] = round(graph_timed(rf, args.steps, dev) * 1e3, 2)
+        res[f"tokens_{n}"] = row
+        del sets
+        torch.cuda.empty_cache()
+    return res
+
+
 def bench_e2e(args, world):
     """configs[1] end to end (the third part of the metric; the reference's
     bench.py:8-28 workload through its own engine): nvattn.e2e runs the fused
@@ -1275,6 +1325,8 @@ def run_only(args):
         res = bench_decode_prepare(dev, args)
     elif args.only == "store":
         res = bench_store_kvcache(dev, args, hbm_peak)
+    elif args.only == "store_sweep":
+        res = bench_store_sweep(dev, args)
     elif args.only == "decode_small":
         res = bench_decode_e2e_shape(dev, args, hbm_peak, batches=(args.batch,))
     elif args.only == "e2e":
@@ -1304,7 +1356,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--skip-secondary", action="store_true")
     ap.add_argument("--only", choices=("prefill", "tree", "qknorm", "sampler", "layer", "prep",
-                                       "store", "e2e", "decode_small"),
+                                       "store", "store_sweep", "e2e", "decode_small"),
                     default=None,
                     help="run just one secondary workload and print its line (for profiling)")
     ap.add_argument("--skip-cpu", action="store_true")
