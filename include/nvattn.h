@@ -238,10 +238,13 @@ NVATTN_API int nvattn_paged_decode_noalloc(const void* q, int64_t q_stride_tok, 
  *   q, out [total_q][num_heads][head_dim]; caches and block_table as in
  *   nvattn_varlen_prefill's paged mode; tree_mask [total_q] uint64.
  *
- * When the sequences alone give too few CTAs, the context is split across
- * CTAs and merged: the fp32 partials go to `workspace` (device, 256-byte
- * aligned, >= nvattn_tree_workspace_bytes of the same sizes; 0 bytes means
- * no split and NULL is accepted). The split depends only on host-side sizes.
+ * `workspace` (device, 256-byte aligned, >= nvattn_tree_workspace_bytes of
+ * the same sizes) holds the order in which sequences are dispatched, longest
+ * first (written by a small kernel on every call, for up to 1024 sequences),
+ * and, when the (sequence, KV head) items are fewer than the SMs, the fp32
+ * partials of the context split across CTAs, which a second kernel merges.
+ * 0 bytes (more than 1024 sequences and no split) accepts NULL. The split
+ * depends only on host-side sizes, so a captured graph keeps its grid.
  */
 NVATTN_API size_t nvattn_tree_workspace_bytes(int32_t num_seqs, int32_t max_nodes, int64_t total_q,
                                               int32_t num_heads, int32_t num_kv_heads,
