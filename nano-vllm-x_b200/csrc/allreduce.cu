@@ -38,9 +38,15 @@
 namespace nvattn {
 
 constexpr int kArMaxRanks = 8;
-constexpr int kArThreads = 512;
+#ifndef NVATTN_AR_THREADS
+#define NVATTN_AR_THREADS 512
+#endif
+#ifndef NVATTN_AR_VECS_PER_THREAD
+#define NVATTN_AR_VECS_PER_THREAD 2
+#endif
+constexpr int kArThreads = NVATTN_AR_THREADS;
 constexpr int kArMaxBlocks = 120;
-constexpr int kArVecsPerThread = 2;  // 16-byte vectors per thread and rank, loads in flight
+constexpr int kArVecsPerThread = NVATTN_AR_VECS_PER_THREAD;  // 16-byte vectors per thread and rank in flight
 constexpr size_t kArHeaderBytes = 4096;
 
 struct ArHeader {
