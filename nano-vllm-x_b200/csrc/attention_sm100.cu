@@ -64,8 +64,15 @@ constexpr uint32_t kTmemCols = 512;
 __device__ __forceinline__ uint32_t col_s(int i) { return static_cast<uint32_t>(i) * 128u; }
 __device__ __forceinline__ uint32_t col_o(int i) { return 256u + static_cast<uint32_t>(i) * 128u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
-constexpr int kPolyEvery = 4;  // lean tiles: 1 exp2 pair in 4 from the FMA-pipe polynomial
-constexpr int kPrefetch = 3;   // key tiles of L2 prefetch ahead of the ring
+// Lean tiles take 1 exp2 pair in this many from the FMA-pipe polynomial instead
+// of MUFU (measured: prefill 785/875/896/890/895 TFLOP/s and tree 724/760/763/
+// 779/781 for 1 in 2/3/4/6/8; the tree's two passes leave the FMA pipe busier).
+constexpr int kPolyEveryPrefill = 4;
+constexpr int kPolyEveryTree = 8;
+#ifndef NVATTN_L2_PREFETCH_TILES
+#define NVATTN_L2_PREFETCH_TILES 3
+#endif
+constexpr int kPrefetch = NVATTN_L2_PREFETCH_TILES;  // key tiles of L2 prefetch ahead of the ring
 
 enum Mode { kDense = 0, kPaged = 1, kTree = 2 };
 
@@ -143,6 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first half overlaps the softmax of the second (measured: +4% on tree,
   // -2% on prefill, which keeps one hand-off).
   constexpr bool kSplitP = MODE == kTree;
+  constexpr int kPolyEvery = MODE == kTree ? kPolyEveryTree : kPolyEveryPrefill;
 
   // ------------------------------------------------ sequence geometry
   const int q_begin = p.cu_q[b];
