@@ -477,6 +477,8 @@ def bench_prefill(dev, rank, world, args, tf_peak):
     for _ in range(args.warmup):
         fn()
     barrier(world)
+    # eager launches: GPU-bound at every N (a call is >= 0.1 ms per rank); under
+    # graph replay the back-to-back calls reach the power cap sooner
     ms = max_over_ranks(timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps,
                         world)
     total = sum_over_ranks(flops, world)
@@ -486,6 +488,7 @@ def bench_prefill(dev, rank, world, args, tf_peak):
            "frac_of_measured_bf16_peak_per_gpu": round(tfs / world / tf_peak, 4),
            "frac_of_measured_bf16_sustained_peak_per_gpu": round(tfs / world / load_peaks()[2], 4),
            "flops_per_step": total,
+           "timing": "CUDA events around back-to-back eager calls, max over ranks",
            "workload": "configs[2]: 64 seqs, 2048-token shared prefix (8 blocks), suffix "
                        "U[128,512], 32Q/8KV, d128, causal over prefix+suffix"}
     if world == 1:
@@ -550,7 +553,7 @@ def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
     for _ in range(args.warmup):
         fn()
     barrier(world)
-    ms = max_over_ranks(timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps,
+    ms = max_over_ranks(graph_timed(fn, max(3, args.steps // 10), dev),
                         world)
     tf = sum_over_ranks(flops, world) / (ms * 1e-3) / 1e12
     gbs = sum_over_ranks(nbytes, world) / (ms * 1e-3) / 1e9
@@ -570,7 +573,7 @@ def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
     for _ in range(args.warmup):
         fn_l()
     barrier(world)
-    ms_l = max_over_ranks(timed(fn_l, args.steps, torch.cuda.current_stream(dev)) / args.steps,
+    ms_l = max_over_ranks(graph_timed(fn_l, max(3, args.steps // 10), dev),
                           world)
     nbytes_l = float(int(ctx.sum() + B * NL) * KVH * D * 2 * 2)
     return {"metric": "tree-verify attn TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
@@ -578,6 +581,7 @@ def bench_tree(dev, rank, world, args, tf_peak, hbm_peak):
             "frac_of_measured_bf16_peak_per_gpu": round(tf / world / tf_peak, 4),
             "frac_of_measured_bf16_sustained_peak_per_gpu": round(tf / world / load_peaks()[2], 4),
             "frac_of_measured_hbm_per_gpu": round(gbs / world / hbm_peak, 4),
+            "timing": "device time per call: 10 calls per CUDA graph, max over ranks",
             "workload": "configs[4]: 32 seqs, ctx U[1024,8192], 64-node tree (branching "
                         "[4,3,2,1,1,1], depth 6), 32Q/8KV, d128",
             "linear_draft_8": {
@@ -893,13 +897,14 @@ def bench_qknorm(dev, rank, world, args, hbm_peak):
     for _ in range(args.warmup):
         fn()
     barrier(world)
-    ms = max_over_ranks(timed(fn, args.steps, torch.cuda.current_stream(dev)) / args.steps,
+    ms = max_over_ranks(graph_timed(fn, max(3, args.steps // 10), dev),
                         world)
     gbs = sum_over_ranks(nbytes, world) / (ms * 1e-3) / 1e9
     res = {"metric": "fused q/k-norm+rotary+KV-scatter GB/s", "value": round(gbs, 1),
            "unit": "GB/s", "ms_per_step": round(ms, 4),
            "frac_of_measured_hbm_per_gpu": round(gbs / world / hbm_peak, 4),
            "bytes_per_step": sum_over_ranks(nbytes, world),
+           "timing": "device time per call: 10 calls per CUDA graph, max over ranks",
            "workload": "Qwen3-0.6B prefill chunk: 16384 tokens, 16Q/8KV, d128, random slots"}
     if world == 1:
         res["reference_four_launch"] = _reference_qknorm(dev, args, pos, q, k, v, w, cos_sin, kc,
