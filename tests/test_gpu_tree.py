@@ -136,3 +136,32 @@ def test_tree_split_and_unsplit_paths():
         ref = R.tree_attention(q, kc, vc, cq.numpy(), ctx, all_masks, bt.numpy(), 128 ** -0.5)
         assert_close(out, ref)
     assert ops.read_status() == 0
+
+
+def test_tree_row_max_growing_in_a_late_tile():
+    """Context keys scaled x10 at positions 200, 300 and 470 (the second half of
+    key tile 1, the first half of tile 2, the second half of tile 3) make many
+    rows' running maxima grow past the rescale threshold after their first
+    tile: the single pass must take the two-pass fallback (first half) or wait
+    for the first half's P V, rescale and redo the second half."""
+    parents, _ = tree.build_draft_tree((4, 3, 2, 1, 1, 1), 64)
+    masks = tree.ancestor_masks(parents)
+    ctx = [700, 700, 520]
+    n = [64] * len(ctx)
+    H, KVH = 32, 8
+    g, kc, vc, q, bt = _setup(ctx, n, H, KVH, 57)
+    for b in range(len(ctx)):
+        for pos in (200, 300, 470):
+            kc[int(bt[b, pos // 256]), pos % 256] = (kc[int(bt[b, pos // 256]), pos % 256].float()
+                                                      * 10).to(torch.bfloat16)
+    all_masks = np.concatenate([masks] * len(ctx))
+    cq = cu(n)
+    out = ops.tree_attention(q.to(dev), kc.to(dev), vc.to(dev), cq.to(dev),
+                             torch.tensor(ctx, dtype=torch.int32, device=dev),
+                             torch.from_numpy(all_masks.view(np.int64)).to(dev), bt.to(dev), 64,
+                             softmax_scale=128 ** -0.5)
+    torch.cuda.synchronize()
+    ref = R.tree_attention(q, kc, vc, cq.numpy(), ctx, all_masks, bt.numpy(), 128 ** -0.5)
+    assert torch.isfinite(out.float()).all()
+    assert_close(out, ref, "tree, late max growth")
+    assert ops.read_status() == 0
