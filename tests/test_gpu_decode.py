@@ -126,6 +126,37 @@ def test_wide_block_table_and_graph_capture():
     assert ops.read_status() == 0
 
 
+def test_many_short_sequences_with_empty_rows():
+    """1000 sequences of 0-299 keys, 30% of them empty (CUDA-graph padding)."""
+    rng = np.random.default_rng(21)
+    lens = rng.integers(0, 300, size=1000)
+    lens[rng.random(1000) < 0.3] = 0
+    out, ref = _run(lens.tolist(), 4, 2, seed=21)
+    assert torch.all(out[torch.from_numpy(lens == 0)] == 0)
+    assert_close(out, ref)
+    assert ops.read_status() == 0
+
+
+def test_one_long_sequence_group16():
+    """One sequence of 60,000 keys, 16 query heads per KV head (both accumulator
+    row halves of the MMA carry heads), split over many CTAs."""
+    out, ref = _run([60000], 16, 1, seed=23)
+    assert_close(out, ref)
+
+
+def test_wide_block_table_with_partials():
+    """64 sequences under a 64-block-wide table: several key splits per pair,
+    most of them past their sequence's end."""
+    rng = np.random.default_rng(24)
+    lens = rng.integers(1, 8000, size=64).tolist()
+    width = 64
+    assert ops.decode_workspace_bytes(64, 16, 8, width, 256) > 0
+    nb = max(1, (max(lens) + 255) // 256)
+    out, ref = _run(lens, 16, 8, seed=24, extra_width=width - nb)
+    assert_close(out, ref)
+    assert ops.read_status() == 0
+
+
 def test_flash_attn_with_kvcache_signature():
     """The keyword form used at attention.py:72-74 returns (B, 1, H, d)."""
     g = torch.Generator().manual_seed(14)
