@@ -386,8 +386,13 @@ NVATTN_API int nvattn_decode_prepare(const void* packed_host, void* packed_dev, 
  * nvattn_ar_buffer_bytes(capacity_elems) with nvattn_ar_alloc (zeroed; it
  * returns the 64-byte CUDA IPC handle), the ranks exchange handles, and each
  * rank opens its peers' with nvattn_ar_open. A buffer is a 4096-byte header
- * of flags followed by two data halves of capacity_elems bf16 each; calls
- * alternate between the halves.
+ * of flags, two data halves of capacity_elems bf16 each, then two receive
+ * areas of 8 slots (one per sending rank) of 16 bytes per 4 elements of
+ * min(capacity_elems, 262144); calls alternate between the halves and areas.
+ * Small messages (at most 262144 elements and (world - 1) * 4 * num_elems
+ * bytes of pushed traffic within 2 MiB) are pushed into the peers' receive
+ * areas with the launch number beside every 4-byte word; larger ones are
+ * published in the rank's own half and read by the peers.
  *
  * Per call: `in` holds the rank's partial (num_elems bf16, written by earlier
  * work on `stream`); buffers[p] is rank p's buffer as mapped in this process

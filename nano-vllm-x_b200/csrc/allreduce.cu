@@ -28,6 +28,19 @@
 // the wait limit (about a second by default) it records
 // NVATTN_STATUS_TIMEOUT and the kernel finishes; that launch's output is then
 // not valid.
+//
+// Messages up to NVATTN_AR_LL_MAX_ELEMS whose push traffic stays small take a
+// second protocol, allreduce_ll_kernel, that carries its flags inside the
+// data: every 4-byte word of the message travels in one 64-bit store together
+// with the launch number e, so a word is valid as soon as it is seen with e,
+// and neither a fence nor a flag round trip nor a read over NVLink lies on
+// the path. Each rank pushes its input into its slot of every peer's receive
+// area (half e % 2, a slot per sending rank), then waits for every peer's
+// words of the same lines in its own memory and sums them in rank order. The
+// two halves make overwriting safe by the argument above: a rank reaches
+// launch e + 2 only after its launch e + 1 saw every peer's launch-e+1
+// words, which a peer pushes only after its own launch e completed. Both
+// protocols share the launch count and give the same bits.
 #include <string.h>
 
 #include <algorithm>
@@ -44,7 +57,19 @@ constexpr int kArMaxRanks = 8;
 #ifndef NVATTN_AR_VECS_PER_THREAD
 #define NVATTN_AR_VECS_PER_THREAD 2
 #endif
+#ifndef NVATTN_AR_LL_MAX_ELEMS
+#define NVATTN_AR_LL_MAX_ELEMS 262144
+#endif
+#ifndef NVATTN_AR_LL_MAX_TRAFFIC
+#define NVATTN_AR_LL_MAX_TRAFFIC (2 << 20)
+#endif
+#ifndef NVATTN_AR_LL_THREADS
+#define NVATTN_AR_LL_THREADS 256
+#endif
 constexpr int kArThreads = NVATTN_AR_THREADS;
+constexpr int64_t kArLLMaxElems = NVATTN_AR_LL_MAX_ELEMS;       // largest message of the LL protocol
+constexpr int64_t kArLLMaxTraffic = NVATTN_AR_LL_MAX_TRAFFIC;   // push bytes per rank it may cost
+constexpr int kArLLThreads = NVATTN_AR_LL_THREADS;
 constexpr int kArMaxBlocks = 120;
 constexpr int kArVecsPerThread = NVATTN_AR_VECS_PER_THREAD;  // 16-byte vectors per thread and rank in flight
 constexpr size_t kArHeaderBytes = 4096;
@@ -218,6 +243,115 @@ __global__ void __launch_bounds__(kArThreads)
   }
 }
 
+__device__ __forceinline__ void st_sys_v2u64(void* p, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ void ld_sys_v2u64(const void* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Four bf16 of the message starting at element 4 * line (zeros past n).
+__device__ __forceinline__ uint2 ll_read_line(const __nv_bfloat16* in, int64_t line, int64_t n) {
+  const int64_t e0 = line * 4;
+  if (e0 + 4 <= n) return reinterpret_cast<const uint2*>(in)[line];
+  const unsigned short* in16 = reinterpret_cast<const unsigned short*>(in);
+  uint32_t h[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) h[k] = (e0 + k < n) ? in16[e0 + k] : 0u;
+  return make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+}
+
+__device__ __forceinline__ void ll_add(float acc[4], uint2 w, bool first) {
+  const float v[4] = {__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u),
+                      __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xffff0000u)};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = first ? v[k] : acc[k] + v[k];
+}
+
+// LL protocol. A line is 16 bytes of a receive slot: two 64-bit words, each
+// {4 bytes of the message, launch number e}, so 8 bytes of message per line.
+// Receive area of a rank: two halves of kArMaxRanks slots (one per sending
+// rank) of slot_bytes each, at ll_off in its buffer.
+__global__ void __launch_bounds__(kArLLThreads)
+    allreduce_ll_kernel(const ArPeers peers, int rank, int world, int64_t n, int64_t ll_off,
+                        int64_t slot_bytes, const __nv_bfloat16* in, __nv_bfloat16* out,
+                        int32_t* status, long long wait_limit) {
+  ArHeader* mine = reinterpret_cast<ArHeader*>(peers.base[rank]);
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    s_epoch = *reinterpret_cast<volatile uint32_t*>(&mine->epoch) + 1u;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int64_t area = ll_off + static_cast<int64_t>(e & 1u) * kArMaxRanks * slot_bytes;
+  const int64_t lines = (n + 3) / 4;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t tag = static_cast<uint64_t>(e) << 32;
+
+  // push this rank's lines into its slot of every peer's receive area
+  for (int64_t i = first; i < lines; i += stride) {
+    const uint2 w = ll_read_line(in, i, n);
+    const uint64_t a = tag | w.x, b = tag | w.y;
+#pragma unroll
+    for (int p = 0; p < kArMaxRanks; ++p)
+      if (p < world && p != rank)
+        st_sys_v2u64(peers.base[p] + area + static_cast<int64_t>(rank) * slot_bytes + i * 16, a, b);
+  }
+
+  // the same lines from every rank, summed in rank order (fp32, one rounding)
+  bool ok = true;
+  const long long t0 = clock64();
+  for (int64_t i = first; i < lines; i += stride) {
+    const uint2 own = ll_read_line(in, i, n);
+    float acc[4];
+#pragma unroll
+    for (int p = 0; p < kArMaxRanks; ++p) {
+      if (p >= world) break;
+      uint2 w = own;
+      if (p != rank) {
+        const char* src = peers.base[rank] + area + static_cast<int64_t>(p) * slot_bytes + i * 16;
+        uint64_t a = 0, b = 0;
+        while (ok) {
+          ld_sys_v2u64(src, a, b);
+          if ((a >> 32) == e && (b >> 32) == e) break;
+          if (clock64() - t0 > wait_limit) ok = false;
+        }
+        w = make_uint2(static_cast<uint32_t>(a), static_cast<uint32_t>(b));
+      }
+      ll_add(acc, w, p == 0);
+    }
+    const int64_t e0 = i * 4;
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc[0], acc[1]);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(acc[2], acc[3]);
+    if (e0 + 4 <= n) {
+      reinterpret_cast<uint2*>(out)[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo),
+                                                    *reinterpret_cast<const uint32_t*>(&hi));
+    } else {
+      const __nv_bfloat16 v[4] = {lo.x, lo.y, hi.x, hi.y};
+      for (int k = 0; k < 4 && e0 + k < n; ++k) out[e0 + k] = v[k];
+    }
+    if (!ok) break;
+  }
+  if (!ok) s_ok = 0;
+  __syncthreads();
+  if (!s_ok && threadIdx.x == 0 && status) atomicOr(status, NVATTN_STATUS_TIMEOUT);
+
+  // the last block of this rank records launch e
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(&mine->done, 1u);
+    if (prev == gridDim.x - 1) {
+      *reinterpret_cast<volatile uint32_t*>(&mine->done) = 0u;
+      *reinterpret_cast<volatile uint32_t*>(&mine->epoch) = e;
+      __threadfence();
+    }
+  }
+}
+
 static int ar_sms() {
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -234,9 +368,17 @@ static size_t ar_half_bytes(int64_t capacity_elems) {
   return (static_cast<size_t>(capacity_elems) * 2 + 15) / 16 * 16;
 }
 
+// Bytes of one LL receive slot: a 16-byte line per 4 elements of the largest
+// LL message the buffer takes.
+static size_t ar_ll_slot_bytes(int64_t capacity_elems) {
+  const int64_t cap = std::min<int64_t>(capacity_elems, kArLLMaxElems);
+  return static_cast<size_t>((cap + 3) / 4) * 16;
+}
+
 extern "C" NVATTN_API size_t nvattn_ar_buffer_bytes(int64_t capacity_elems) {
   if (capacity_elems < 0) return 0;
-  return kArHeaderBytes + 2 * ar_half_bytes(capacity_elems);
+  return kArHeaderBytes + 2 * ar_half_bytes(capacity_elems) +
+         2 * kArMaxRanks * ar_ll_slot_bytes(capacity_elems);
 }
 
 extern "C" NVATTN_API int64_t nvattn_ar_set_wait_limit(int64_t cycles) {
@@ -316,6 +458,22 @@ extern "C" NVATTN_API int nvattn_allreduce(const uint64_t* buffers, int32_t rank
   if ((o + bytes > own && o < own_end) || (i + bytes > own && i < own_end))
     return fail(NVATTN_ERR_INVALID, "allreduce: in or out overlaps the shared buffer");
   if (num_elems == 0) return NVATTN_OK;
+  const int64_t ll_cap = std::min<int64_t>(capacity_elems, kArLLMaxElems);
+  if (num_elems <= ll_cap && (world - 1) * num_elems * 4 <= kArLLMaxTraffic) {
+    const int64_t lines = (num_elems + 3) / 4;
+    int64_t grid = (lines + kArLLThreads - 1) / kArLLThreads;
+    grid = std::max<int64_t>(1, std::min<int64_t>(grid, ar_sms()));
+    allreduce_ll_kernel<<<static_cast<unsigned>(grid), kArLLThreads, 0,
+                          reinterpret_cast<cudaStream_t>(stream)>>>(
+        peers, rank, world, num_elems,
+        static_cast<int64_t>(kArHeaderBytes + 2 * ar_half_bytes(capacity_elems)),
+        static_cast<int64_t>(ar_ll_slot_bytes(capacity_elems)),
+        static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), status,
+        g_ar_wait_limit.load());
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "allreduce_ll_kernel");
+    return NVATTN_OK;
+  }
   const int64_t nvec = num_elems / 8;
   const int64_t per_launch = static_cast<int64_t>(kArThreads) * kArVecsPerThread;
   int64_t grid = (nvec + per_launch - 1) / per_launch;

@@ -5,7 +5,8 @@ bf16 rounding) bit for bit, and NCCL's dist.all_reduce (bit for bit at two
 ranks, where NCCL's bf16 sum is one rounded add; closely beyond); every rank
 holds the same bits; a captured CUDA graph with two launches replays with new
 inputs; hundreds of back-to-back calls of alternating sizes keep the flags in
-step; and RowParallelLinear.forward through it (linear.py:152-155) equals
+step, also when calls switch between the two protocols; and
+RowParallelLinear.forward through it (linear.py:152-155) equals
 F.linear + the oracle's sum. Also reports the per-call time against NCCL from
 4 KB to 2 MB. Skipped with fewer GPUs than ranks.
 """
@@ -110,14 +111,20 @@ def _worker(rank, world, port, paths, result_q):
             twice = R.allreduce_sum(np.stack([once] * world))
             checks.append(np.array_equal(_bits(out), twice))
         del graph
-        # many calls in a row: flags and launch counts stay in step
+        # many calls in a row: flags and launch counts stay in step, with the
+        # sizes (and at two ranks the protocol: pushed words up to 256 K
+        # elements, published halves beyond) changing from call to call
+        big = 300_001
         g = torch.Generator(device=dev).manual_seed(7 + rank)
-        mine = (torch.randn(n, generator=g, device=dev)).to(torch.bfloat16)
-        want = oracle_sum(mine)
-        for i in range(300):  # alternating sizes: chunk boundaries move between launches
-            m = n if i % 2 == 0 else 4099
-            ar.all_reduce(mine[:m], out[:m])
-        checks.append(np.array_equal(_bits(out), want))
+        mine = (torch.randn(big, generator=g, device=dev)).to(torch.bfloat16)
+        wide = torch.empty(big, dtype=torch.bfloat16, device=dev)
+        sizes = (n, 4099, big)
+        for i in range(300):  # chunk boundaries move between launches
+            m = sizes[i % 3]
+            ar.all_reduce(mine[:m], wide[:m])
+            if i % 50 == 49 or i == 298:
+                checks.append(np.array_equal(_bits(wide[:m]), oracle_sum(mine[:m])))
+        checks.append(np.array_equal(_bits(wide), oracle_sum(mine)))
         # RowParallelLinear.forward through the one-shot all-reduce
         g = torch.Generator(device=dev).manual_seed(11 + rank)
         x = (torch.randn(256, 1024, generator=g, device=dev)).to(torch.bfloat16)

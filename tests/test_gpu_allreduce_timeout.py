@@ -7,10 +7,10 @@ With the wait limit shortened to about a millisecond, the launch must end
 by itself and set NVATTN_STATUS_TIMEOUT. No peer GPU is involved, every
 address is a local allocation, and the context stays usable.
 
-Rank 1 then calls with its own input: rank 0's chunks of that launch are
-already published, so rank 1's waits succeed at once and its output must be
-the exact sum of both ranks' inputs. The flags stayed consistent through the
-timed-out launch.
+Rank 1 then calls with its own input: rank 0's part of that launch is
+already published (or pushed), so rank 1's waits succeed at once and its
+output must be the exact sum of both ranks' inputs. The flags stayed
+consistent through the timed-out launch. Both protocols are covered.
 """
 from __future__ import annotations
 
@@ -32,9 +32,12 @@ def _bits(t):
     return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def test_wait_on_a_peer_that_never_arrives_times_out():
+@pytest.mark.parametrize("cap", [300_001, 100_001], ids=["published-halves", "pushed-words"])
+def test_wait_on_a_peer_that_never_arrives_times_out(cap):
+    """300,001 elements take the protocol whose ranks publish their own half
+    and read the peers'; 100,001 the one that pushes every word with the
+    launch number into the peers' receive areas."""
     lib = _lib.load()
-    cap = 300_001
     nbytes = lib.nvattn_ar_buffer_bytes(cap)
     bufs = []
     try:

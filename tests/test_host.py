@@ -97,7 +97,8 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     # one-shot all-reduce: argument checks before any launch
     import ctypes as C
     bufs = (C.c_uint64 * 2)(0x10000, 0x20000)
-    assert lib.nvattn_ar_buffer_bytes(1000) == 4096 + 2 * 2000     # header + two halves
+    # header + two halves + two LL receive areas of 8 slots (a 16-byte line per 4 elements)
+    assert lib.nvattn_ar_buffer_bytes(1000) == 4096 + 2 * 2000 + 2 * 8 * 250 * 16
     x = C.c_void_p(0x40000)
     assert lib.nvattn_allreduce(C.addressof(bufs), 0, 0, 8, 8, x, fake, None, None) == _lib.ERR_INVALID
     assert lib.nvattn_allreduce(C.addressof(bufs), 2, 2, 8, 8, x, fake, None, None) == _lib.ERR_INVALID
