@@ -790,6 +790,9 @@ def bench_e2e(args, world):
             line = json.loads(r.stdout.strip().splitlines()[-1])
             res[arm] = {"value": line["value"], "seconds": line["seconds"],
                         "output_tokens": line["output_tokens"]}
+            if arm == "nvattn-fused" and world > 1:
+                # decode-sized row-parallel all-reduces through nvattn's peer-memory kernel
+                res[arm]["peer_memory_allreduce"] = bool(line.get("oneshot_allreduce"))
             outs[arm] = out
         if len(outs) == 2:
             sys.path.insert(0, str(REPO / "nano-vllm-x_b200"))

@@ -390,7 +390,7 @@ NVATTN_API int nvattn_decode_prepare(const void* packed_host, void* packed_dev, 
  * areas of 8 slots (one per sending rank) of 16 bytes per 4 elements of
  * min(capacity_elems, 262144); calls alternate between the halves and areas.
  * Small messages (at most 262144 elements and (world - 1) * 4 * num_elems
- * bytes of pushed traffic within 2 MiB) are pushed into the peers' receive
+ * bytes of pushed traffic within 4 MiB) are pushed into the peers' receive
  * areas with the launch number beside every 4-byte word; larger ones are
  * published in the rank's own half and read by the peers.
  *
@@ -424,6 +424,14 @@ NVATTN_API int nvattn_allreduce(const uint64_t* buffers, int32_t rank, int32_t w
  * wait on a peer that never arrives end with NVATTN_STATUS_TIMEOUT.
  */
 NVATTN_API int64_t nvattn_ar_set_wait_limit(int64_t cycles);
+/*
+ * Which protocol nvattn_allreduce takes for num_elems over world ranks with
+ * buffers of capacity_elems: 1 = words pushed into the peers' receive areas
+ * (small messages; the faster one), 0 = halves published and read by the
+ * peers, -1 = such a call is invalid. Lets a caller keep another all-reduce
+ * for the sizes where this one is not the faster.
+ */
+NVATTN_API int32_t nvattn_ar_protocol(int32_t world, int64_t num_elems, int64_t capacity_elems);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "nvattn_ar_free": (c_int, [_P]),
     "nvattn_allreduce": (c_int, [_P, c_int32, c_int32, c_int64, c_int64, _P, _P, _I32P, _P]),
     "nvattn_ar_set_wait_limit": (c_int64, [c_int64]),
+    "nvattn_ar_protocol": (c_int32, [c_int32, c_int64, c_int64]),
     "nvattn_decode_prepare_bytes": (c_size_t, [c_int64, c_int32]),
     "nvattn_decode_prepare": (c_int, [_P, _P, c_int64, c_int32, c_int32, c_int64,
                                       _P, _P, _I32P, _I32P, _I32P, c_int64, _I32P, _P]),

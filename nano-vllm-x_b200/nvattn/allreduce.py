@@ -4,11 +4,13 @@ RowParallelLinear.forward (nanovllm/layers/linear.py:152-155) computes
 ``y = F.linear(x, W_shard)`` on every rank and sums the partials with
 ``dist.all_reduce(y)`` (NCCL). For decode-sized messages (a few hundred
 tokens x hidden) NCCL's per-call latency dominates. Here one kernel
-(``nvattn_allreduce``) copies each rank's partial into its IPC-shared buffer,
-synchronises with the peers through per-block flags in those buffers, reads
-every partial over NVLink and writes the sum: the same bits on every rank, the
-single rounded bf16 add of NCCL's sum at two ranks. Messages larger than the
-buffer keep NCCL, the reference's own collective.
+(``nvattn_allreduce``) sums the partials over the ranks' IPC-shared buffers:
+small messages are pushed into every peer's receive area with the launch
+number beside each 4-byte word (no fence or flag round trip), larger ones are
+published in the rank's own buffer behind per-block flags and read by the
+peers over NVLink. Either way every rank gets the same bits, the single
+rounded bf16 add of NCCL's sum at two ranks. Messages larger than the buffer
+keep NCCL, the reference's own collective.
 """
 from __future__ import annotations
 
@@ -91,6 +93,11 @@ class OneShotAllReduce:
                   status.data_ptr() if status is not None else None, _stream(self.device))
         return out
 
+    def pushes_words(self, numel: int) -> bool:
+        """True when a call of numel elements takes the pushed-words protocol
+        (the one faster than NCCL; nvattn_ar_protocol)."""
+        return _lib.load().nvattn_ar_protocol(self.world, int(numel), self.capacity) == 1
+
     def close(self) -> None:
         """Release the mappings and the buffer (collective: all ranks)."""
         if self._closed:
@@ -107,15 +114,19 @@ class OneShotAllReduce:
 
 
 def row_parallel_forward(ar: OneShotAllReduce, x: torch.Tensor, weight: torch.Tensor,
-                         bias: torch.Tensor | None, tp_rank: int) -> torch.Tensor | None:
+                         bias: torch.Tensor | None, tp_rank: int,
+                         pushed_only: bool = False) -> torch.Tensor | None:
     """RowParallelLinear.forward (linear.py:152-155) through the one-shot
     all-reduce: the rank's F.linear partial, then one kernel sums it across
-    ranks in place. Returns None when the message exceeds the buffer (the
-    caller keeps the reference path)."""
+    ranks in place. Returns None when the message exceeds the buffer, or with
+    pushed_only when it would not take the pushed-words protocol (the caller
+    keeps the reference path)."""
     import torch.nn.functional as F
     n_out = weight.shape[0]
     numel = x.numel() // x.shape[-1] * n_out
     if numel == 0 or numel > ar.capacity:
+        return None
+    if pushed_only and not ar.pushes_words(numel):
         return None
     y = F.linear(x, weight, bias if tp_rank == 0 else None)
     return ar.all_reduce(y.contiguous())

@@ -29,10 +29,11 @@ The engine is used unchanged except for what this environment lacks:
   each decode step's metadata comes from one packed host record and one
   kernel writing the CUDA graph's inputs in place
   (``nvattn.DecodeMetadata``, replacing prepare_decode and run_model's
-  copies, model_runner.py:172-188, 204-210); with ``--oneshot-allreduce``
-  (off by default: slower than NCCL so far) the row-parallel linears'
-  all-reduce at TP > 1 runs through nvattn's one-shot peer-memory kernel
-  (``nvattn.allreduce``, linear.py:152-155) for decode-sized messages;
+  copies, model_runner.py:172-188, 204-210); and at TP > 1 the row-parallel
+  linears' all-reduce (linear.py:152-155) runs through nvattn's peer-memory
+  kernel (``nvattn.allreduce``) for the messages it pushes word by word
+  (decode steps), NCCL keeping the larger ones (``--nccl-allreduce`` keeps
+  NCCL for all; ``--oneshot-allreduce`` is the default, kept as a flag);
   ``--attn reference`` keeps the engine's own flash-attn / Triton path.
 
     python -m nvattn.e2e --tp 1 --attn nvattn [--num-seqs 256] [--out ids.npz] [--record]
@@ -146,8 +147,9 @@ _ONESHOT_CAPACITY = 512 * 4096  # decode graphs up to 512 tokens x hidden 4096
 
 def _row_parallel_oneshot_forward(self, x):
     """RowParallelLinear.forward (linear.py:152-155) at TP > 1 through
-    nvattn's one-shot peer-memory all-reduce; messages larger than its buffer
-    keep the reference's F.linear + dist.all_reduce."""
+    nvattn's peer-memory all-reduce for the messages it pushes word by word
+    (decode steps); larger ones keep the reference's F.linear +
+    dist.all_reduce."""
     global _ONESHOT
     if self.tp_size == 1:
         return self._reference_forward(x)
@@ -155,7 +157,7 @@ def _row_parallel_oneshot_forward(self, x):
         from nvattn.allreduce import OneShotAllReduce
         _ONESHOT = OneShotAllReduce(_ONESHOT_CAPACITY)
     from nvattn.allreduce import row_parallel_forward
-    y = row_parallel_forward(_ONESHOT, x, self.weight, self.bias, self.tp_rank)
+    y = row_parallel_forward(_ONESHOT, x, self.weight, self.bias, self.tp_rank, pushed_only=True)
     return y if y is not None else self._reference_forward(x)
 
 
@@ -341,8 +343,11 @@ def bench_workload(num_seqs: int = 256, max_input_len: int = 1024, max_output_le
 
 def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: int,
         enforce_eager: bool, model_dir: str | None = None, out: str | None = None,
-        oneshot_allreduce: bool = False, record: bool = False,
+        oneshot_allreduce: bool | None = None, record: bool = False,
         max_num_seqs: int | None = None) -> dict:
+    if oneshot_allreduce is None:  # the default: on for the fused arm at TP > 1
+        oneshot_allreduce = attn == "nvattn-fused" and tp > 1
+    oneshot_allreduce = bool(oneshot_allreduce and attn == "nvattn-fused" and tp > 1)
     os.environ["NVATTN_E2E_ATTN"] = attn
     os.environ["NVATTN_E2E_ONESHOT_AR"] = "1" if oneshot_allreduce else "0"
     os.environ["NVATTN_E2E_RECORD"] = "1" if record else "0"
@@ -474,9 +479,12 @@ def main() -> None:
     ap.add_argument("--model-dir", default=None, help="reuse a written model directory")
     ap.add_argument("--write-model", default=None, help="only write the model to this dir")
     ap.add_argument("--out", default=None, help="save generated token ids (npz)")
-    ap.add_argument("--oneshot-allreduce", action="store_true",
-                    help="fused arm at TP > 1: row-parallel all-reduce through nvattn's "
-                         "peer-memory kernel instead of NCCL")
+    ar = ap.add_mutually_exclusive_group()
+    ar.add_argument("--oneshot-allreduce", dest="oneshot", action="store_true", default=None,
+                    help="fused arm at TP > 1: row-parallel all-reduce of decode-sized "
+                         "messages through nvattn's peer-memory kernel (the default)")
+    ar.add_argument("--nccl-allreduce", dest="oneshot", action="store_false",
+                    help="fused arm at TP > 1: keep NCCL for every row-parallel all-reduce")
     ap.add_argument("--record", action="store_true",
                     help="keep the top-2 logits of every generated token (saved by --out)")
     ap.add_argument("--max-num-seqs", type=int, default=None,
@@ -498,7 +506,7 @@ def main() -> None:
         write_model(Path(args.write_model))
         return
     res = run(args.tp, args.attn, args.num_seqs, args.max_input_len, args.max_output_len,
-              args.enforce_eager, args.model_dir, args.out, args.oneshot_allreduce, args.record,
+              args.enforce_eager, args.model_dir, args.out, args.oneshot, args.record,
               args.max_num_seqs)
     print(json.dumps(res), flush=True)
 

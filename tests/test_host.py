@@ -118,6 +118,12 @@ def test_c_abi_rejects_bad_arguments_before_any_launch():
     prev = lib.nvattn_ar_set_wait_limit(1000)
     assert prev == 2_000_000_000 and lib.nvattn_ar_set_wait_limit(0) == 1000
     assert lib.nvattn_ar_set_wait_limit(0) == 2_000_000_000         # 0 restored the default
+    # protocol choice: pushed words while (world - 1) * 4 * n <= 4 MiB and n <= 262144
+    assert lib.nvattn_ar_protocol(2, 256 * 1024, 1 << 20) == 1
+    assert lib.nvattn_ar_protocol(2, 256 * 1024 + 1, 1 << 20) == 0
+    assert lib.nvattn_ar_protocol(4, 256 * 1024, 1 << 20) == 1
+    assert lib.nvattn_ar_protocol(8, 149796, 1 << 20) == 1 and lib.nvattn_ar_protocol(8, 149797, 1 << 20) == 0
+    assert lib.nvattn_ar_protocol(4, 1000, 999) == -1 and lib.nvattn_ar_protocol(9, 8, 8) == -1
     assert lib.nvattn_ar_alloc(10, None, None) == _lib.ERR_INVALID
     assert lib.nvattn_ar_open(None, None) == _lib.ERR_INVALID
     assert lib.nvattn_ar_close(None) == _lib.OK and lib.nvattn_ar_free(None) == _lib.OK
