@@ -2,7 +2,7 @@
 //
 // Everything here is hand-written inline PTX for the Blackwell data path:
 // mbarrier pipelines, TMA tensor loads (cp.async.bulk.tensor, never with
-// .multicast::cluster), ldmatrix and the bf16 tensor-core MMAs.
+// cluster multicast), ldmatrix and the bf16 tensor-core MMAs.
 #pragma once
 
 #include <cuda.h>
