@@ -59,12 +59,27 @@ __device__ __forceinline__ uint4 philox4x32_10(uint32_t c0, uint32_t c1, uint32_
 // k = x >> 9. k + 0.5 < 2^23 needs 24 significant bits, so u is exact in
 // fp32 and lies in [2^-24, 1 - 2^-24]: -log u > 0 and the noise is finite
 // (with 24 bits, k + 0.5 would round to 2^24 for the largest k, u to 1 and
-// the noise to +inf). Then -log(-log u). The inner log is the accurate logf:
-// near u = 1, -log u is ~6e-8 and an approximate log's absolute error would
-// swamp it.
+// the noise to +inf). Then -log(-log u).
+//
+// The inner -log u needs relative accuracy where it is small (u near 1: the
+// largest noise values, the ones that win). t = 1 - u is exact in fp32 (u is
+// an odd multiple of 2^-24: for u >= 1/2 by Sterbenz's lemma, below that 1 - u
+// lies in [1/2, 1), where the spacing is 2^-24), and -log u = -log1p(-t) =
+// t + t^2/2 + t^3/3 + ...:
+// for t < 1/32 five terms leave a relative error below t^5/6 < 6e-9. For
+// t >= 1/32, -log u >= 0.031 and the MUFU log (absolute error ~2^-22 in
+// log2) is within 6e-6 relative, so the noise moves by less than 6e-6: far
+// below the bf16 spacing of the logits it is added to, and every path and
+// shard computes it the same way.
 __device__ __forceinline__ float gumbel(uint32_t x) {
   const float u = (static_cast<float>(x >> 9) + 0.5f) * 1.1920928955078125e-07f;  // 2^-23
-  return -__logf(-logf(u));
+  const float t = 1.0f - u;
+  float p = fmaf(t, 0.2f, 0.25f);
+  p = fmaf(t, p, 0.333333343f);
+  p = fmaf(t, p, 0.5f);
+  p = fmaf(t, p, 1.0f);
+  const float e = t < 0.03125f ? t * p : -__logf(u);
+  return -__logf(e);
 }
 
 // No gumbel() value exceeds this: the largest u = 1 - 2^-24 gives
