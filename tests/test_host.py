@@ -295,3 +295,36 @@ def test_e2e_compare_finds_first_divergence_and_reference_margin(tmp_path):
     # 2.0 - 1.984375 = 2^-6 = 1 ulp of 2.0 in bf16 (8 significant bits)
     assert row["ref_margin_ulps"] == 1.0
     assert res["diverged_within_k"] == 1
+
+
+def test_split_policies_from_host_sizes():
+    """The split choices of decode and tree verification depend only on host
+    sizes (a captured graph keeps its grid); their workspace sizes expose them.
+    Without a GPU the SM count reads as 148 (B200). A partial slot is 128 fp32
+    of O plus a (max, sum) pair: 520 bytes."""
+    lib = _lib.load()
+    slot = 128 * 4 + 8
+
+    def dec(B, H, KVH, W, BS=256):
+        return lib.nvattn_decode_workspace_bytes(B, H, KVH, W, BS)
+
+    # configs[3] at TP1: 128 x 8 pairs fill >= 8 CTAs per SM with 64-tile
+    # (4096-key) splits of the 512-tile table: 8 splits
+    assert dec(128, 64, 8, 128) == 128 * 64 * 8 * slot
+    # one KV head per GPU (TP8): 128 pairs need 32-tile splits: 16 of them
+    assert dec(128, 8, 1, 128) == 128 * 8 * 16 * slot
+    # the e2e batch of 256 over a 16-block table: one split covers it, no merge
+    assert dec(256, 16, 8, 16) == 0
+    # batch 16: the smallest split (4 tiles), 8 per pair over an 8-block table
+    assert dec(16, 16, 8, 8) == 16 * 16 * 8 * slot
+
+    def tree(S, N, H, KVH, W, BS=256):
+        return lib.nvattn_tree_workspace_bytes(S, N, S * N, H, KVH, W, BS)
+
+    order = 256  # 32 int32 sequence indices, 256-byte aligned
+    # configs[4]: 256 (sequence, KV head) items >= 148 SMs: no split, order only
+    assert tree(32, 64, 32, 8, 33) == order
+    # TP2 shard: 128 items -> 2 splits; TP8 shard: 32 items -> 5, doubled under a
+    # quarter of the SMs, capped at 66 tiles / 8 = 8 splits
+    assert tree(32, 64, 16, 4, 33) == order + 32 * 64 * 16 * 2 * slot
+    assert tree(32, 64, 4, 1, 33) == order + 32 * 64 * 4 * 8 * slot
