@@ -328,3 +328,40 @@ def test_split_policies_from_host_sizes():
     # quarter of the SMs, capped at 66 tiles / 8 = 8 splits
     assert tree(32, 64, 16, 4, 33) == order + 32 * 64 * 16 * 2 * slot
     assert tree(32, 64, 4, 1, 33) == order + 32 * 64 * 4 * 8 * slot
+
+
+def test_row_parallel_forward_routing():
+    """row_parallel_forward keeps the caller's NCCL path (returns None) before any
+    GPU work when the message exceeds the buffer, or, with pushed_only, when
+    it would not take the pushed-word protocol."""
+    from nvattn.allreduce import row_parallel_forward
+
+    class FakeAR:
+        capacity = 4096
+
+        def __init__(self, pushed):
+            self.pushed = pushed
+            self.calls = 0
+
+        def pushes_words(self, numel):
+            return self.pushed
+
+        def all_reduce(self, y):
+            self.calls += 1
+            return y
+
+    x = torch.randn(8, 64)
+    w = torch.randn(1024, 64)             # 8 x 1024 = 8192 elements > capacity
+    ar = FakeAR(True)
+    assert row_parallel_forward(ar, x, w, None, 0) is None and ar.calls == 0
+    x = torch.randn(2, 64)                # 2048 elements
+    ar = FakeAR(False)
+    assert row_parallel_forward(ar, x, w, None, 0, pushed_only=True) is None and ar.calls == 0
+    y = row_parallel_forward(ar, x, w, None, 0)            # published halves are fine here
+    assert ar.calls == 1 and torch.equal(y, torch.nn.functional.linear(x, w))
+    ar = FakeAR(True)
+    b = torch.randn(1024)
+    y1 = row_parallel_forward(ar, x, w, b, 1, pushed_only=True)   # bias only on rank 0
+    assert ar.calls == 1 and torch.equal(y1, torch.nn.functional.linear(x, w))
+    y0 = row_parallel_forward(ar, x, w, b, 0, pushed_only=True)
+    assert torch.equal(y0, torch.nn.functional.linear(x, w, b))
