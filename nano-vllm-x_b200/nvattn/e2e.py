@@ -341,13 +341,20 @@ def bench_workload(num_seqs: int = 256, max_input_len: int = 1024, max_output_le
     return prompts, max_tokens
 
 
+def peer_memory_allreduce(attn: str, tp: int, requested: bool | None) -> bool:
+    """Whether a run routes its decode-sized row-parallel all-reduces through
+    nvattn's peer-memory kernel: only the fused arm at TP > 1 can, and it does
+    unless the caller asked for NCCL (requested False); None is the default."""
+    if attn != "nvattn-fused" or tp <= 1:
+        return False
+    return True if requested is None else bool(requested)
+
+
 def run(tp: int, attn: str, num_seqs: int, max_input_len: int, max_output_len: int,
         enforce_eager: bool, model_dir: str | None = None, out: str | None = None,
         oneshot_allreduce: bool | None = None, record: bool = False,
         max_num_seqs: int | None = None) -> dict:
-    if oneshot_allreduce is None:  # the default: on for the fused arm at TP > 1
-        oneshot_allreduce = attn == "nvattn-fused" and tp > 1
-    oneshot_allreduce = bool(oneshot_allreduce and attn == "nvattn-fused" and tp > 1)
+    oneshot_allreduce = peer_memory_allreduce(attn, tp, oneshot_allreduce)
     os.environ["NVATTN_E2E_ATTN"] = attn
     os.environ["NVATTN_E2E_ONESHOT_AR"] = "1" if oneshot_allreduce else "0"
     os.environ["NVATTN_E2E_RECORD"] = "1" if record else "0"

@@ -365,3 +365,11 @@ def test_row_parallel_forward_routing():
     assert ar.calls == 1 and torch.equal(y1, torch.nn.functional.linear(x, w))
     y0 = row_parallel_forward(ar, x, w, b, 0, pushed_only=True)
     assert torch.equal(y0, torch.nn.functional.linear(x, w, b))
+
+
+def test_e2e_allreduce_default():
+    from nvattn.e2e import peer_memory_allreduce as pm
+    assert pm("nvattn-fused", 2, None) and pm("nvattn-fused", 8, None)
+    assert not pm("nvattn-fused", 2, False) and pm("nvattn-fused", 4, True)
+    assert not pm("nvattn-fused", 1, None) and not pm("nvattn-fused", 1, True)
+    assert not pm("nvattn", 2, None) and not pm("reference", 2, True)
